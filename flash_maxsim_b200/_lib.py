@@ -1,0 +1,130 @@
+"""ctypes binding of libflashmaxsim_sm100.so (C ABI: include/flash_maxsim_sm100.h).
+
+The library must exist: importing this module without it raises ImportError.
+There is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+from .build import LIB_PATH
+
+FM_OK = 0
+FM_ERR_ARG = 1
+FM_ERR_LAUNCH = 2
+FM_ERR_TIMEOUT_SELFTEST = 19
+FM_ERR_BAD_INDEX = 20
+FM_ERR_UNSUPPORTED = 21
+FM_DTYPE_F16 = 0
+FM_DTYPE_F32 = 1
+FM_DTYPE_BF16 = 2
+
+# exported symbol -> (restype, argtypes)
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+SIGNATURES = {
+    "fm_abi_version": (_I, []),
+    "fm_status_string": (ctypes.c_char_p, [_I]),
+    "fm_set_wait_timeout_ns": (None, [_I64]),
+    "fm_maxsim_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "fm_maxsim_int8_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "fm_maxsim_sparse_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "fm_maxsim_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "fm_quantize_int8": (_I, [_P, _I, _P, _P, _P, _I64, _I, _P]),
+    "fm_wait_selftest": (_I, [_P, _I64, _P]),
+    "fm_fwd_plan_info": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I]),
+}
+
+PLAN_FIELDS = ("C", "G", "nd", "nq", "nu", "nk", "kq_atoms", "d_atoms", "RS", "rep",
+               "q_resident", "nts", "ts_stride", "smem", "R")
+
+
+def plan_info(mode: int, argmax: bool, Nq: int, B: int, Lq: int, Ld: int, d: int,
+              shared: bool = True, K: int = 0) -> dict:
+    """The forward launch plan for a shape (mode 0 dense, 1 sparse, 2 INT8)."""
+    out = (ctypes.c_int32 * len(PLAN_FIELDS))()
+    rc = lib.fm_fwd_plan_info(mode, int(argmax), Nq, B, Lq, Ld, d, int(shared), K,
+                              ctypes.cast(out, ctypes.c_void_p), len(PLAN_FIELDS))
+    check(rc, "fm_fwd_plan_info")
+    return dict(zip(PLAN_FIELDS, list(out)))
+
+
+def _load() -> ctypes.CDLL:
+    path = Path(os.environ.get("FLASH_MAXSIM_LIB", LIB_PATH))
+    if not path.exists():
+        raise ImportError(
+            f"{path} is missing: build it with `python flash_maxsim_b200/build.py` "
+            "(flash_maxsim_b200 has no non-CUDA implementation)"
+        )
+    lib = ctypes.CDLL(str(path))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+LOADED_PATH = Path(lib._name)
+
+
+def status_string(code: int) -> str:
+    return lib.fm_status_string(int(code)).decode()
+
+
+def check(rc: int, what: str) -> None:
+    """Raise for a host-side error code returned by an entry point."""
+    if rc != FM_OK:
+        msg = f"{what}: {status_string(rc)} (code {rc})"
+        if rc == FM_ERR_ARG:
+            raise ValueError(msg)
+        raise RuntimeError(msg)
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 status word that kernels write device-side errors into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def sync_check_enabled() -> bool:
+    return os.environ.get("FLASH_MAXSIM_SYNC_CHECK", "0") not in ("", "0")
+
+
+def check_status(device: torch.device | int | None = None) -> None:
+    """Synchronise `device` and raise RuntimeError if a kernel recorded an error.
+
+    Device-side failures (a bounded wait that ran out of time, an index out of
+    range) do not abort the CUDA context; they are recorded in the status word
+    and reported here. The word is cleared after it has been read.
+    """
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    st = status_word(device)
+    torch.cuda.synchronize(device)
+    code = int(st.item())
+    if code != FM_OK:
+        st.zero_()
+        raise RuntimeError(f"flash_maxsim_b200 device error: {status_string(code)} (code {code})")

@@ -1,0 +1,353 @@
+"""Public MaxSim API, call-compatible with flash_maxsim 0.1.0 (flash_maxsim/__init__.py:3-5).
+
+Every scoring function runs the hand-written sm_100a kernels of
+libflashmaxsim_sm100.so; inputs must be CUDA tensors (there is no CPU path).
+`maxsim_naive`, `maxsim_sparse_naive` and `dequantize_int8` are the
+reference's plain-torch helpers and stay plain torch, as in the reference.
+
+Error behaviour follows the reference: shape mismatches raise AssertionError
+(flash_maxsim/flash_maxsim.py:223,236,239,242; flash_maxsim_quant.py:22,113;
+flash_maxsim_sparse.py:115,119); a host-side launch error raises
+RuntimeError / ValueError; device-side errors land in the status word read by
+`check_status()`.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from ._lib import lib
+
+
+# ---------------------------------------------------------------------------
+# input preparation
+# ---------------------------------------------------------------------------
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError(
+                "flash_maxsim_b200 scores CUDA tensors only (the kernels are sm_100a CUDA); "
+                f"got a tensor on {t.device}"
+            )
+
+
+def _pad_last(t: torch.Tensor, mult: int) -> torch.Tensor:
+    d = t.shape[-1]
+    pad = (-d) % mult
+    return F.pad(t, (0, pad)) if pad else t
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _half(t: torch.Tensor, mult: int = 8) -> torch.Tensor:
+    """Reference casting (`.contiguous().half()`), plus zero padding of the
+    embedding dimension to a multiple of `mult` (zeros add nothing to a dot
+    product) and 16-byte alignment for TMA."""
+    return _aligned(_pad_last(t.half(), mult))
+
+
+def _lengths(doc_lengths, n: int, Ld: int, device) -> torch.Tensor | None:
+    # _default_lengths (flash_maxsim/flash_maxsim.py:211-214); None means "all Ld"
+    if doc_lengths is None:
+        return None
+    if not torch.is_tensor(doc_lengths):
+        doc_lengths = torch.as_tensor(doc_lengths)
+    lens = doc_lengths.to(device=device, dtype=torch.int32).contiguous()
+    assert lens.numel() == n, f"doc_lengths has {lens.numel()} entries, expected {n}"
+    return lens
+
+
+def _after_call(device):
+    if _lib.sync_check_enabled():
+        _lib.check_status(device)
+
+
+def _fwd(Q3: torch.Tensor, D2: torch.Tensor, lengths, Nq, B, Lq, Ld, shared: bool,
+         save_argmax: bool):
+    """Launch fm_maxsim_fwd. Q3: [Nq, Lq, d'] fp16, D2: [docs, Ld, d'] fp16."""
+    dev = Q3.device
+    scores = torch.empty(Nq, B, device=dev, dtype=torch.float32)
+    argmax = (torch.empty(Nq * B, Lq, device=dev, dtype=torch.int32) if save_argmax else None)
+    if B == 0:
+        return scores, argmax
+    d = Q3.shape[-1]
+    with torch.cuda.device(dev):
+        rc = lib.fm_maxsim_fwd(
+            Q3.data_ptr(), D2.data_ptr(), _lib.ptr(lengths), scores.data_ptr(),
+            _lib.ptr(argmax), Nq, B, Lq, Ld, d, 1 if shared else 0,
+            _lib.status_word(dev).data_ptr(), _lib.stream_of(dev))
+    _lib.check(rc, "fm_maxsim_fwd")
+    _after_call(dev)
+    return scores, argmax
+
+
+def _degenerate(Nq, B, Lq, Ld, device):
+    """Scores when the kernel has nothing to do: no query tokens sum to 0,
+    no document tokens give max = -inf (as the reference's loops do)."""
+    if Lq == 0:
+        return torch.zeros(Nq, B, device=device, dtype=torch.float32)
+    return torch.full((Nq, B), float("-inf"), device=device, dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# fp16 forward (flash_maxsim/flash_maxsim.py:221-250)
+# ---------------------------------------------------------------------------
+
+def flash_maxsim(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None) -> torch.Tensor:
+    """Compute MaxSim scores. Q: [Lq, d], D: [B, Ld, d] -> [B] fp32.
+
+    score[b] = sum_q max_{t < doc_lengths[b]} <Q[q], D[b, t]>; inputs are cast
+    to fp16 like the reference (flash_maxsim/flash_maxsim.py:221-230).
+    """
+    assert Q.dim() == 2 and D.dim() == 3 and Q.shape[1] == D.shape[2]
+    _require_cuda(Q, D)
+    Lq, d = Q.shape
+    B, Ld, _ = D.shape
+    lengths = _lengths(doc_lengths, B, Ld, D.device)
+    if Lq == 0 or Ld == 0:
+        return _degenerate(1, B, Lq, Ld, D.device).squeeze(0)
+    Q3 = _half(Q.unsqueeze(0))
+    D2 = _half(D)
+    scores, _ = _fwd(Q3, D2, lengths, 1, B, Lq, Ld, True, False)
+    return scores.squeeze(0)
+
+
+def flash_maxsim_batched(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None,
+                         shared_docs: bool = True) -> torch.Tensor:
+    """Batched MaxSim. Q: [Nq, Lq, d], D: [B, Ld, d] -> [Nq, B] fp32.
+
+    shared_docs=False takes per-query documents D: [Nq, B, Ld, d] and
+    doc_lengths of Nq*B entries (flash_maxsim/flash_maxsim.py:233-250).
+    Every document is read from HBM once for the whole query batch.
+    """
+    assert Q.dim() == 3 and Q.shape[2] == D.shape[-1]
+    _require_cuda(Q, D)
+    Nq, Lq, d = Q.shape
+    if shared_docs:
+        assert D.dim() == 3
+        B, Ld, _ = D.shape
+    else:
+        assert D.dim() == 4 and D.shape[0] == Nq
+        _, B, Ld, _ = D.shape
+        D = D.reshape(Nq * B, Ld, d)
+    total = B if shared_docs else Nq * B
+    lengths = _lengths(doc_lengths, total, Ld, D.device)
+    if Nq == 0:
+        return torch.empty(0, B, device=D.device, dtype=torch.float32)
+    if Lq == 0 or Ld == 0:
+        return _degenerate(Nq, B, Lq, Ld, D.device)
+    scores, _ = _fwd(_half(Q), _half(D), lengths, Nq, B, Lq, Ld, shared_docs, False)
+    return scores
+
+
+# ---------------------------------------------------------------------------
+# training (flash_maxsim/flash_maxsim.py:253-291)
+# ---------------------------------------------------------------------------
+
+class _FlashMaxSimFn(torch.autograd.Function):
+    """Forward saves the per-row argmax; backward scatters/gathers through it
+    (the reference's _FlashMaxSimFn, flash_maxsim/flash_maxsim.py:253-286),
+    extended to query batches and variable-length documents."""
+
+    @staticmethod
+    def forward(ctx, Q, D, doc_lengths):
+        single = Q.dim() == 2
+        Q3 = Q.unsqueeze(0) if single else Q
+        Nq, Lq, d = Q3.shape
+        B, Ld, _ = D.shape
+        Qh = _half(Q3)
+        Dh = _half(D)
+        lengths = _lengths(doc_lengths, B, Ld, D.device)
+        scores, argmax = _fwd(Qh, Dh, lengths, Nq, B, Lq, Ld, True, True)
+        ctx.save_for_backward(Qh, Dh, argmax)
+        ctx.meta = (single, Nq, B, Lq, Ld, d, Q.dtype, D.dtype)
+        return scores.squeeze(0) if single else scores
+
+    @staticmethod
+    def backward(ctx, grad_scores):
+        Qh, Dh, argmax = ctx.saved_tensors
+        single, Nq, B, Lq, Ld, d, q_dtype, d_dtype = ctx.meta
+        g = grad_scores.reshape(Nq, B).contiguous().float()
+        dp = Qh.shape[-1]
+        grad_Q = torch.empty(Nq, Lq, dp, device=Qh.device, dtype=torch.float16)
+        grad_D = torch.empty(B, Ld, dp, device=Dh.device, dtype=torch.float16)
+        dev = Qh.device
+        with torch.cuda.device(dev):
+            rc = lib.fm_maxsim_bwd(
+                Qh.data_ptr(), Dh.data_ptr(), argmax.data_ptr(), g.data_ptr(),
+                grad_Q.data_ptr(), grad_D.data_ptr(), Nq, B, Lq, Ld, dp, _lib.stream_of(dev))
+        _lib.check(rc, "fm_maxsim_bwd")
+        _after_call(dev)
+        grad_Q = grad_Q[..., :d]
+        grad_D = grad_D[..., :d]
+        if single:
+            grad_Q = grad_Q.squeeze(0)
+        gq = grad_Q.to(q_dtype) if ctx.needs_input_grad[0] else None
+        gd = grad_D.to(d_dtype) if ctx.needs_input_grad[1] else None
+        return gq, gd, None
+
+
+def flash_maxsim_train(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None) -> torch.Tensor:
+    """MaxSim with autograd backward. Q: [Lq, d] -> [B] (reference signature),
+    or Q: [Nq, Lq, d] -> [Nq, B]; D: [B, Ld, d]; optional doc_lengths [B].
+
+    Gradients: dQ[q] = sum_b g_b D[b, argmax], dD[b, argmax] += g_b Q[q],
+    accumulated in fp32 in a fixed order and returned in the input dtype.
+    """
+    assert Q.dim() in (2, 3) and D.dim() == 3 and Q.shape[-1] == D.shape[2]
+    _require_cuda(Q, D)
+    assert Q.shape[-2] >= 1 and D.shape[1] >= 1
+    return _FlashMaxSimFn.apply(Q, D, doc_lengths)
+
+
+def maxsim_naive(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None) -> torch.Tensor:
+    """Reference PyTorch MaxSim (flash_maxsim/flash_maxsim.py:294-301).
+    Q: [Lq, d], D: [B, Ld, d] -> [B]; fp32 einsum, -inf past doc_lengths."""
+    sim = torch.einsum("qd,bld->bql", Q.float(), D.float())
+    if doc_lengths is not None:
+        pos = torch.arange(D.shape[1], device=D.device)
+        mask = pos[None, None, :] >= doc_lengths.to(D.device)[:, None, None]
+        sim = sim.masked_fill(mask, float("-inf"))
+    return sim.max(dim=2).values.sum(dim=1)
+
+
+# ---------------------------------------------------------------------------
+# INT8 (flash_maxsim/flash_maxsim_quant.py)
+# ---------------------------------------------------------------------------
+
+_QDTYPE = {torch.float16: _lib.FM_DTYPE_F16, torch.float32: _lib.FM_DTYPE_F32,
+           torch.bfloat16: _lib.FM_DTYPE_BF16}
+
+
+def quantize_int8(D: torch.Tensor):
+    """Per-token affine INT8 quantisation (flash_maxsim/flash_maxsim_quant.py:11-28).
+
+    D: [B, Ld, d] -> (uint8 [B, Ld, d], scales fp16 [B, Ld, 1], mins fp16 [B, Ld, 1]),
+    bit-identical to the reference formula, computed by one CUDA kernel pass.
+    """
+    assert D.dim() == 3
+    _require_cuda(D)
+    B, Ld, d = D.shape
+    x = D if D.dtype in _QDTYPE else D.float()
+    # the kernel reads 8 elements per lane: pad rows with their own first
+    # element (changes neither min nor max), then drop the padded columns
+    pad = (-d) % 8
+    if pad:
+        x = torch.cat([x, x[..., :1].expand(B, Ld, pad)], dim=-1)
+    x = _aligned(x)
+    dp = d + pad
+    u8 = torch.empty(B, Ld, dp, device=D.device, dtype=torch.uint8)
+    scales = torch.empty(B, Ld, 1, device=D.device, dtype=torch.float16)
+    mins = torch.empty(B, Ld, 1, device=D.device, dtype=torch.float16)
+    rows = B * Ld
+    if rows:
+        with torch.cuda.device(D.device):
+            rc = lib.fm_quantize_int8(x.data_ptr(), _QDTYPE[x.dtype], u8.data_ptr(),
+                                      scales.data_ptr(), mins.data_ptr(), rows, dp,
+                                      _lib.stream_of(D.device))
+        _lib.check(rc, "fm_quantize_int8")
+        _after_call(D.device)
+    if pad:
+        u8 = u8[..., :d].contiguous()
+    return u8, scales, mins
+
+
+def dequantize_int8(D_uint8: torch.Tensor, scales: torch.Tensor, mins: torch.Tensor) -> torch.Tensor:
+    """Reconstruct fp32 values u * scale + min (flash_maxsim/flash_maxsim_quant.py:31-33)."""
+    return D_uint8.float() * scales.float() + mins.float()
+
+
+def flash_maxsim_int8(Q: torch.Tensor, D_uint8: torch.Tensor, scales: torch.Tensor,
+                      mins: torch.Tensor, doc_lengths=None) -> torch.Tensor:
+    """Fused dequant + MaxSim. Q: [Lq, d], D_uint8: [B, Ld, d] -> [B] fp32
+    (flash_maxsim/flash_maxsim_quant.py:105-142). scales/mins: [B, Ld, 1] or [B, Ld].
+
+    The tensor cores multiply Q by the exact integers u; the per-token map
+    scale * <q, u> + min * sum(q) is applied in fp32 in the epilogue.
+    """
+    assert Q.dim() == 2 and D_uint8.dim() == 3 and Q.shape[1] == D_uint8.shape[2]
+    _require_cuda(Q, D_uint8, scales, mins)
+    Lq, d = Q.shape
+    B, Ld, _ = D_uint8.shape
+    if scales.dim() == 3:
+        scales = scales.squeeze(-1)
+    if mins.dim() == 3:
+        mins = mins.squeeze(-1)
+    lengths = _lengths(doc_lengths, B, Ld, D_uint8.device)
+    if Lq == 0 or Ld == 0:
+        return _degenerate(1, B, Lq, Ld, D_uint8.device).squeeze(0)
+    # zero-padding both Q and the codes keeps every dot product unchanged
+    Qh = _half(Q, 16)
+    Du = _aligned(_pad_last(D_uint8.to(torch.uint8), 16))
+    sc = _aligned(scales.half())
+    mn = _aligned(mins.half())
+    assert sc.shape == (B, Ld) and mn.shape == (B, Ld)
+    scores = torch.empty(B, device=Q.device, dtype=torch.float32)
+    if B == 0:
+        return scores
+    dev = Q.device
+    with torch.cuda.device(dev):
+        rc = lib.fm_maxsim_int8_fwd(Qh.data_ptr(), Du.data_ptr(), sc.data_ptr(), mn.data_ptr(),
+                                    _lib.ptr(lengths), scores.data_ptr(), B, Lq, Ld,
+                                    Qh.shape[-1], _lib.status_word(dev).data_ptr(),
+                                    _lib.stream_of(dev))
+    _lib.check(rc, "fm_maxsim_int8_fwd")
+    _after_call(dev)
+    return scores
+
+
+# ---------------------------------------------------------------------------
+# sparse (flash_maxsim/flash_maxsim_sparse.py)
+# ---------------------------------------------------------------------------
+
+def flash_maxsim_sparse(Q: torch.Tensor, D: torch.Tensor, indices: torch.Tensor,
+                        doc_lengths=None) -> torch.Tensor:
+    """Sparse MaxSim with per-doc query-token selection
+    (flash_maxsim/flash_maxsim_sparse.py:98-140).
+
+    Q: [Lq, d] shared query, D: [B, Ld, d], indices: [B, K] query-token ids per
+    doc, doc_lengths: optional [B]. Returns [B] fp32:
+    score[b] = sum_k max_{t < len_b} <Q[indices[b, k]], D[b, t]>.
+    """
+    assert Q.dim() == 2 and D.dim() == 3 and indices.dim() == 2
+    _require_cuda(Q, D, indices)
+    Lq, d = Q.shape
+    B, Ld, _ = D.shape
+    _, K = indices.shape
+    assert indices.shape[0] == B
+    lengths = _lengths(doc_lengths, B, Ld, D.device)
+    if K == 0:
+        return torch.zeros(B, device=D.device, dtype=torch.float32)
+    if Ld == 0:
+        return torch.full((B,), float("-inf"), device=D.device, dtype=torch.float32)
+    assert Lq >= 1
+    Qh = _half(Q)
+    Dh = _half(D)
+    idx = indices.to(torch.int32).contiguous()
+    scores = torch.empty(B, device=D.device, dtype=torch.float32)
+    if B == 0:
+        return scores
+    dev = D.device
+    with torch.cuda.device(dev):
+        rc = lib.fm_maxsim_sparse_fwd(Qh.data_ptr(), Dh.data_ptr(), idx.data_ptr(),
+                                      _lib.ptr(lengths), scores.data_ptr(), B, K, Lq, Ld,
+                                      Qh.shape[-1], _lib.status_word(dev).data_ptr(),
+                                      _lib.stream_of(dev))
+    _lib.check(rc, "fm_maxsim_sparse_fwd")
+    _after_call(dev)
+    return scores
+
+
+def maxsim_sparse_naive(Q: torch.Tensor, D: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+    """Reference sparse MaxSim (flash_maxsim/flash_maxsim_sparse.py:143-157).
+    Q: [Lq, d], D: [B, Ld, d], indices: [B, K] -> [B] (no length masking)."""
+    q_sel = Q[indices.long()]
+    sim = torch.einsum("bkd,bld->bkl", q_sel.float(), D.float())
+    return sim.max(dim=2).values.sum(dim=1)

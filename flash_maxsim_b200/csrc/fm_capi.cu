@@ -1,0 +1,394 @@
+// C ABI of libflashmaxsim_sm100.so: argument checks, launch plans, TMA
+// descriptors and kernel launches.  Declarations: include/flash_maxsim_sm100.h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/flash_maxsim_sm100.h"
+#include "fm_aux.cuh"
+#include "fm_fwd.cuh"
+
+namespace fm {
+namespace {
+
+constexpr int kMaxSmem = 232448;        // 227 KB opt-in shared memory per CTA on sm_100
+constexpr int kMinSmem = 120 * 1024;    // keeps one CTA per SM (each owns all 512 TMEM columns)
+std::atomic<int64_t> g_timeout_ns{2000000000LL};
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+int cdiv(int x, int m) { return (x + m - 1) / m; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  static int cache[64] = {0};
+  if (dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 3D tiled map over a [n2][n1][n0] tensor, box {b0, b1, 1}
+bool make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t n0,
+                 uint64_t n1, uint64_t n2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {n0, n1, n2};
+  cuuint64_t strides[2] = {n0 * esize, n0 * n1 * esize};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct Shape {
+  int mode;
+  bool argmax;
+  int Nq, B, Lq, Ld, d, K;
+  int shared;
+};
+
+// Choose chunk size, ring depths and shared-memory carve-up.
+bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
+  const bool int8 = s.mode == MODE_INT8;
+  a.Nq = s.Nq;
+  a.B = s.B;
+  a.Lq = s.Lq;
+  a.Ld = s.Ld;
+  a.d = s.d;
+  a.K = s.K;
+  a.shared = s.shared;
+  a.Gq = cdiv(s.Lq, 32);
+  a.R = s.shared ? s.Nq * a.Gq : a.Gq;
+  a.n_work = s.shared ? s.B : s.Nq * s.B;
+  a.rep = a.R == 1 ? 4 : (a.R == 2 ? 2 : 1);
+  const int atoms = cdiv(s.d, 64);
+  a.kq_atoms = std::min(atoms, 2);
+  a.nk = cdiv(atoms, a.kq_atoms);
+  a.d_atoms = a.nk * a.kq_atoms;
+  a.d_atoms_real = atoms;
+  // Chunk: the fewest chunks of <= 256 tokens that cover Ld with equal sizes,
+  // capped so that one chunk (all K atoms) plus two Q stages fit in shared memory.
+  if (s.Ld <= 256) {
+    a.C = round_up(std::max(s.Ld, 16), 16);
+  } else {
+    const int n = cdiv(s.Ld, 256);
+    a.C = round_up(cdiv(s.Ld, n), 16);
+  }
+  {
+    const int budget = kMaxSmem - 2 * a.kq_atoms * 16384 - 16 * 1024;
+    const int cap = (budget / (a.d_atoms * 128)) / 16 * 16;
+    if (cap < 16) return false;
+    a.C = std::min(a.C, cap);
+  }
+  a.ts_stride = round_up(a.C, 32);
+  a.nts = 512 / a.ts_stride;
+  a.q_resident = (s.shared && a.R <= 4 && a.nk == 1) ? 1 : 0;
+  a.q_stage_bytes = a.kq_atoms * 16384u;
+  a.d_slot_bytes = static_cast<uint32_t>(a.d_atoms) * a.C * 128u;
+  a.u_slot_bytes = int8 ? static_cast<uint32_t>(a.d_atoms) * a.C * 64u : 0u;
+  a.rowbuf = (s.mode == MODE_SPARSE) ? a.Gq * 32 : a.R;
+  const int nch_max = cdiv(s.Ld, a.C);
+  const int mb_total = cdiv(a.R, 4);
+
+  const int rows_bytes = round_up(a.rowbuf * 4, 16);
+  const int xch_bytes = 128 * 8;
+  const int qsum_bytes = int8 ? round_up(a.Gq * 32 * 4, 16) : 0;
+  const int state_per_mb = 128 * 4 * (s.argmax ? 2 : 1);
+
+  for (int G = nch_max; G >= 1; --G) {
+    if (a.nk > 1 && G > a.nts) continue;
+    const bool multi = G < nch_max;
+    const int nd_hi = a.q_resident && !int8 ? std::max(2 * G, 8) : 2 * G;
+    for (int nd = nd_hi; nd >= G; --nd) {
+      const int nq_hi = a.q_resident ? 1 : 4, nq_lo = a.q_resident ? 1 : 2;
+      for (int nq = nq_hi; nq >= nq_lo; --nq) {
+        const int nu_hi = int8 ? 6 : 0, nu_lo = int8 ? 2 : 0;
+        for (int nu = nu_hi; nu >= nu_lo; --nu) {
+          const int nbars = 2 * nq + 2 * nd + 2 * a.nts + 2 * nu + 1;
+          const int bar_bytes = round_up(nbars * 8 + 16, 16);
+          const int base = 1024 + nq * static_cast<int>(a.q_stage_bytes) +
+                           nd * static_cast<int>(a.d_slot_bytes) + nu * static_cast<int>(a.u_slot_bytes) +
+                           rows_bytes + xch_bytes + qsum_bytes + bar_bytes;
+          if (base > kMaxSmem) continue;
+          int state_bytes = 0;
+          int RS;
+          if (multi && a.rep == 1) {
+            const int fit_mb = (kMaxSmem - base) / state_per_mb;
+            const int mb = std::min(mb_total, fit_mb);
+            if (mb < 1) continue;
+            RS = mb * 4;
+            state_bytes = mb * state_per_mb;
+          } else if (multi) {
+            RS = 4;
+            state_bytes = state_per_mb;
+            if (base + state_bytes > kMaxSmem) continue;
+          } else {
+            RS = round_up(a.R, 4);
+          }
+          a.G = G;
+          a.nd = nd;
+          a.nq = nq;
+          a.nu = nu;
+          a.RS = RS;
+          uint32_t off = 0;
+          a.off_q = off;
+          off += nq * a.q_stage_bytes;
+          a.off_d = off;
+          off += nd * a.d_slot_bytes;
+          a.off_u = off;
+          off += nu * a.u_slot_bytes;
+          a.off_state = off;
+          off += state_bytes;
+          a.off_rows = off;
+          off += rows_bytes;
+          a.off_xch = off;
+          off += xch_bytes;
+          a.off_qsum = off;
+          off += qsum_bytes;
+          a.off_bar = round_up(off, 16);
+          off = a.off_bar + bar_bytes;
+          smem_bytes = std::max(static_cast<int>(off) + 1024, kMinSmem);
+          return smem_bytes <= kMaxSmem;
+        }
+      }
+    }
+  }
+  return false;
+}
+
+template <int MODE, bool ARGMAX>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& td, const FwdArgs& a, int smem,
+               cudaStream_t stream) {
+  auto kern = maxsim_fwd_kernel<MODE, ARGMAX>;
+  static std::atomic<int> configured_smem{0};
+  if (configured_smem.load() < smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+        cudaSuccess)
+      return FM_ERR_LAUNCH;
+    configured_smem.store(kMaxSmem);
+  }
+  const int sms = sm_count();
+  if (sms <= 0) return FM_ERR_NO_DEVICE;
+  const int grid = std::max(1, std::min(a.n_work, sms));
+  const int threads = MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16;
+  kern<<<grid, threads, smem, stream>>>(tq, td, a);
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
+               int32_t* argmax, const int32_t* sp_idx, const void* scales, const void* mins,
+               int32_t* status, cudaStream_t stream) {
+  if (!Q || !D || !scores || !status) return FM_ERR_ARG;
+  if (s.Nq < 1 || s.B < 0 || s.Lq < 1 || s.Ld < 1 || s.d < 8 || s.d > 2048) return FM_ERR_ARG;
+  if (s.d % 8 != 0) return FM_ERR_ARG;
+  if (s.mode == MODE_INT8 && s.d % 16 != 0) return FM_ERR_ARG;
+  if (!aligned16(Q) || !aligned16(D)) return FM_ERR_ARG;
+  if (s.mode == MODE_SPARSE && (s.K < 0 || (s.K > 0 && !sp_idx))) return FM_ERR_ARG;
+  if (s.mode == MODE_INT8 && (!scales || !mins)) return FM_ERR_ARG;
+  if (s.B == 0) return FM_OK;
+  const int64_t n_docs = s.shared ? s.B : static_cast<int64_t>(s.Nq) * s.B;
+  if (n_docs > INT32_MAX || static_cast<int64_t>(s.Nq) * s.B > INT32_MAX) return FM_ERR_ARG;
+
+  FwdArgs a{};
+  int smem = 0;
+  if (!make_plan(s, a, smem)) return FM_ERR_UNSUPPORTED;
+  a.lengths = lengths;
+  a.scores = scores;
+  a.argmax = argmax;
+  a.sp_idx = sp_idx;
+  a.q = static_cast<const __half*>(Q);
+  a.scales = static_cast<const __half*>(scales);
+  a.mins = static_cast<const __half*>(mins);
+  a.status = status;
+  a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
+
+  CUtensorMap tq, td;
+  if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, s.mode == MODE_DENSE ? s.Nq : 1,
+                   64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  if (s.mode == MODE_INT8) {
+    if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, s.d, s.Ld, n_docs, 64, a.C,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return FM_ERR_LAUNCH;
+  } else {
+    if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, s.Ld, n_docs, 64, a.C,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return FM_ERR_LAUNCH;
+  }
+  switch (s.mode) {
+    case MODE_DENSE:
+      return s.argmax ? launch_fwd<MODE_DENSE, true>(tq, td, a, smem, stream)
+                      : launch_fwd<MODE_DENSE, false>(tq, td, a, smem, stream);
+    case MODE_SPARSE:
+      return launch_fwd<MODE_SPARSE, false>(tq, td, a, smem, stream);
+    case MODE_INT8:
+      return launch_fwd<MODE_INT8, false>(tq, td, a, smem, stream);
+  }
+  return FM_ERR_ARG;
+}
+
+}  // namespace
+}  // namespace fm
+
+using namespace fm;
+
+extern "C" {
+
+int fm_abi_version(void) { return 100; }
+
+const char* fm_status_string(int code) {
+  switch (code) {
+    case FM_OK: return "ok";
+    case FM_ERR_ARG: return "invalid argument";
+    case FM_ERR_LAUNCH: return "kernel launch or TMA descriptor error";
+    case FM_ERR_TIMEOUT_DFULL: return "device wait timed out: document tile never arrived";
+    case FM_ERR_TIMEOUT_DEMPTY: return "device wait timed out: document slot never released";
+    case FM_ERR_TIMEOUT_QFULL: return "device wait timed out: query block never arrived";
+    case FM_ERR_TIMEOUT_QEMPTY: return "device wait timed out: query stage never released";
+    case FM_ERR_TIMEOUT_TFULL: return "device wait timed out: accumulator never committed";
+    case FM_ERR_TIMEOUT_TEMPTY: return "device wait timed out: accumulator never drained";
+    case FM_ERR_TIMEOUT_UFULL: return "device wait timed out: uint8 tile never arrived";
+    case FM_ERR_TIMEOUT_UEMPTY: return "device wait timed out: uint8 slot never released";
+    case FM_ERR_TIMEOUT_DRAIN: return "device wait timed out while draining in-flight copies";
+    case FM_ERR_TIMEOUT_SELFTEST: return "device wait timed out (self test)";
+    case FM_ERR_BAD_INDEX: return "sparse query index out of range";
+    case FM_ERR_UNSUPPORTED: return "shape not supported by the sm_100a kernels";
+    case FM_ERR_NO_DEVICE: return "no CUDA device";
+  }
+  return "unknown status";
+}
+
+void fm_set_wait_timeout_ns(int64_t ns) { g_timeout_ns.store(ns > 0 ? ns : 2000000000LL); }
+
+int fm_fwd_plan_info(int mode, int argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
+                     int K, int32_t* out, int n_out) {
+  if (!out || n_out < 15 || mode < 0 || mode > 2) return FM_ERR_ARG;
+  if (Nq < 1 || B < 0 || Lq < 1 || Ld < 1 || d < 8 || d > 2048) return FM_ERR_ARG;
+  Shape s{mode, argmax != 0, Nq, B, Lq, Ld, d, K, shared_docs ? 1 : 0};
+  FwdArgs a{};
+  int smem = 0;
+  if (!make_plan(s, a, smem)) return FM_ERR_UNSUPPORTED;
+  const int32_t v[15] = {a.C, a.G, a.nd, a.nq, a.nu, a.nk, a.kq_atoms, a.d_atoms, a.RS, a.rep,
+                         a.q_resident, a.nts, a.ts_stride, smem, a.R};
+  for (int i = 0; i < 15; ++i) out[i] = v[i];
+  return FM_OK;
+}
+
+int fm_maxsim_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengths, float* scores,
+                  int32_t* argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
+                  int32_t* status, void* stream) {
+  Shape s{MODE_DENSE, argmax != nullptr, Nq, B, Lq, Ld, d, 0, shared_docs ? 1 : 0};
+  return fwd_common(s, Q, D, doc_lengths, scores, argmax, nullptr, nullptr, nullptr, status,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int fm_maxsim_int8_fwd(const uint16_t* Q, const uint8_t* D_u8, const uint16_t* scales,
+                       const uint16_t* mins, const int32_t* doc_lengths, float* scores, int B,
+                       int Lq, int Ld, int d, int32_t* status, void* stream) {
+  Shape s{MODE_INT8, false, 1, B, Lq, Ld, d, 0, 1};
+  return fwd_common(s, Q, D_u8, doc_lengths, scores, nullptr, nullptr, scales, mins, status,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int fm_maxsim_sparse_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* indices,
+                         const int32_t* doc_lengths, float* scores, int B, int K, int Lq, int Ld,
+                         int d, int32_t* status, void* stream) {
+  Shape s{MODE_SPARSE, false, 1, B, Lq, Ld, d, K, 1};
+  return fwd_common(s, Q, D, doc_lengths, scores, nullptr, indices, nullptr, nullptr, status,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
+                  const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
+                  int Lq, int Ld, int d, void* stream) {
+  if (!Q || !D || !argmax || !grad_scores || !grad_Q || !grad_D) return FM_ERR_ARG;
+  if (Nq < 1 || B < 0 || Lq < 1 || Ld < 1 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
+  if (!aligned16(Q) || !aligned16(D) || !aligned16(grad_Q) || !aligned16(grad_D)) return FM_ERR_ARG;
+  const int64_t E = static_cast<int64_t>(Nq) * Lq;
+  if (E > 32768) return FM_ERR_UNSUPPORTED;
+  const size_t smem = (static_cast<size_t>(Ld) + 1 + E) * 4 + static_cast<size_t>(Nq) * 4;
+  if (smem > static_cast<size_t>(kMaxSmem)) return FM_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0) {
+    // no documents: dQ is zero
+    return cudaMemsetAsync(grad_Q, 0, E * d * 2, st) == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+  }
+  dim3 gq(Nq, cdiv(Lq, 8));
+  maxsim_bwd_dq_kernel<<<gq, kBwdThreads, 0, st>>>(
+      reinterpret_cast<const __half*>(D), argmax, grad_scores, reinterpret_cast<__half*>(grad_Q),
+      Nq, B, Lq, Ld, d, 1);
+  if (cudaGetLastError() != cudaSuccess) return FM_ERR_LAUNCH;
+  static std::atomic<bool> dd_cfg{false};
+  if (!dd_cfg.load()) {
+    if (cudaFuncSetAttribute(maxsim_bwd_dd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxSmem) != cudaSuccess)
+      return FM_ERR_LAUNCH;
+    dd_cfg.store(true);
+  }
+  maxsim_bwd_dd_kernel<<<B, kBwdThreads, smem, st>>>(
+      reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D),
+      Nq, B, Lq, Ld, d);
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,
+                     int64_t rows, int d, void* stream) {
+  if (!D || !D_u8 || !scales || !mins || rows < 0 || d < 8 || d > 2048 || d % 8 != 0)
+    return FM_ERR_ARG;
+  if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_u8) & 7u)) return FM_ERR_ARG;
+  if (rows == 0) return FM_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > INT32_MAX) return FM_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned nb = static_cast<unsigned>(blocks);
+  __half* sc = reinterpret_cast<__half*>(scales);
+  __half* mn = reinterpret_cast<__half*>(mins);
+  switch (dtype) {
+    case FM_DTYPE_F16:
+      quantize_int8_kernel<__half><<<nb, 256, 0, st>>>(static_cast<const __half*>(D), D_u8, sc, mn, rows, d);
+      break;
+    case FM_DTYPE_F32:
+      quantize_int8_kernel<float><<<nb, 256, 0, st>>>(static_cast<const float*>(D), D_u8, sc, mn, rows, d);
+      break;
+    case FM_DTYPE_BF16:
+      quantize_int8_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(D), D_u8, sc, mn, rows, d);
+      break;
+    default:
+      return FM_ERR_ARG;
+  }
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int fm_wait_selftest(int32_t* status, int64_t timeout_ns, void* stream) {
+  if (!status || timeout_ns <= 0) return FM_ERR_ARG;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<uint64_t>(timeout_ns));
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+}  // extern "C"

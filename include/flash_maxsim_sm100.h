@@ -1,0 +1,154 @@
+/*
+ * flash_maxsim_sm100.h -- C ABI of libflashmaxsim_sm100.so, the B200 (sm_100a)
+ * MaxSim scoring kernels.
+ *
+ * Plain C: device pointers, sizes and a CUDA stream handle (cudaStream_t
+ * passed as void*). fp16 tensors are passed as uint16_t bit patterns. Every
+ * tensor is dense, row-major and contiguous, with 16-byte-aligned base
+ * addresses. The library allocates nothing: the caller owns every buffer.
+ * Calls are asynchronous on `stream` and re-entrant.
+ *
+ * Return value: 0 on success, otherwise an FM_ERR_* code for an argument or
+ * launch error detected on the host. Device-side failures (a bounded wait that
+ * ran out of time, a sparse index out of range) are written into the caller's
+ * device status word `status` (first error wins; 0 = OK); read it after the
+ * stream has been synchronised. fm_status_string() names every code.
+ *
+ * Each entry point replaces one launch site of the reference (roipony/flash-maxsim
+ * 0.1.0, Triton kernels), cited per function.
+ */
+#ifndef FLASH_MAXSIM_SM100_H
+#define FLASH_MAXSIM_SM100_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status / error codes */
+#define FM_OK 0
+#define FM_ERR_ARG 1
+#define FM_ERR_LAUNCH 2
+/* device-side bounded waits that ran out of time (10..18) */
+#define FM_ERR_TIMEOUT_DFULL 10
+#define FM_ERR_TIMEOUT_DEMPTY 11
+#define FM_ERR_TIMEOUT_QFULL 12
+#define FM_ERR_TIMEOUT_QEMPTY 13
+#define FM_ERR_TIMEOUT_TFULL 14
+#define FM_ERR_TIMEOUT_TEMPTY 15
+#define FM_ERR_TIMEOUT_UFULL 16
+#define FM_ERR_TIMEOUT_UEMPTY 17
+#define FM_ERR_TIMEOUT_DRAIN 18
+#define FM_ERR_TIMEOUT_SELFTEST 19
+#define FM_ERR_BAD_INDEX 20
+#define FM_ERR_UNSUPPORTED 21
+#define FM_ERR_NO_DEVICE 22
+
+/* ABI version of this header (major * 100 + minor). */
+int fm_abi_version(void);
+
+/* Human-readable name of a status / error code. */
+const char* fm_status_string(int code);
+
+/* Limit, in nanoseconds, of every device-side wait (default 2e9). */
+void fm_set_wait_timeout_ns(int64_t ns);
+
+/*
+ * Launch plan the forward entry points would use for a shape (host only, no
+ * device needed). mode: 0 dense, 1 sparse, 2 INT8. Writes 15 ints to `out`:
+ * chunk tokens C, chunks per resident group G, D ring slots, Q ring stages,
+ * INT8 staging slots, Q stages per M-block, K atoms per Q stage, K atoms per
+ * token, row groups per span, lane-quarter replication, Q resident flag, TMEM
+ * slots, TMEM columns per slot, dynamic shared memory bytes, row groups per
+ * work item. No counterpart in the reference (its Triton autotuner picks tile
+ * sizes at run time, flash_maxsim/flash_maxsim.py:15-81).
+ */
+int fm_fwd_plan_info(int mode, int argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
+                     int K, int32_t* out, int n_out);
+
+/*
+ * MaxSim forward, fp16 inputs, fp32 scores.
+ *   scores[n * B + b] = sum_{q<Lq} max_{t<len(doc)} <Q[n,q,:], D[doc,t,:]>
+ * shared_docs = 1: D is [B, Ld, d], doc = b, every query scores every doc.
+ * shared_docs = 0: D is [Nq, B, Ld, d], doc = n * B + b.
+ * doc_lengths: NULL (all Ld) or int32 per doc ([B] shared, [Nq*B] otherwise);
+ *   values are clamped to [0, Ld]; an empty doc scores -inf.
+ * argmax: NULL, or int32 [Nq*B, Lq] receiving the first token index of each
+ *   row maximum (-1 for an empty doc).
+ * Q: [Nq, Lq, d] fp16; d % 8 == 0, d <= 2048.
+ * Replaces the `_launch_fwd` -> `_maxsim_fwd_kernel` launch
+ *   (flash_maxsim/flash_maxsim.py:195-208, kernel :83-146), used by
+ *   flash_maxsim (:221-230), flash_maxsim_batched (:233-250) and the
+ *   training forward (:255-263).
+ */
+int fm_maxsim_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengths,
+                  float* scores, int32_t* argmax, int Nq, int B, int Lq, int Ld, int d,
+                  int shared_docs, int32_t* status, void* stream);
+
+/*
+ * Fused dequantise + MaxSim, single query.
+ *   scores[b] = sum_q max_t sum_k Q[q,k] * (u[b,t,k] * scale[b,t] + min[b,t])
+ * D_u8: [B, Ld, d] uint8 (d % 16 == 0), scales/mins: [B, Ld] fp16.
+ * Replaces `_maxsim_int8_kernel` launched by flash_maxsim_int8
+ *   (flash_maxsim/flash_maxsim_quant.py:105-142, kernel :52-98).
+ */
+int fm_maxsim_int8_fwd(const uint16_t* Q, const uint8_t* D_u8, const uint16_t* scales,
+                       const uint16_t* mins, const int32_t* doc_lengths, float* scores, int B,
+                       int Lq, int Ld, int d, int32_t* status, void* stream);
+
+/*
+ * Sparse MaxSim: per document b, only the K query rows indices[b, :] count
+ * (duplicates count twice, negative indices wrap like torch indexing).
+ *   scores[b] = sum_{k<K} max_{t<len(b)} <Q[indices[b,k],:], D[b,t,:]>
+ * Q: [Lq, d], D: [B, Ld, d], indices: int32 [B, K].
+ * Replaces `_sparse_maxsim_kernel` launched by flash_maxsim_sparse
+ *   (flash_maxsim/flash_maxsim_sparse.py:98-140, kernel :42-91).
+ */
+int fm_maxsim_sparse_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* indices,
+                         const int32_t* doc_lengths, float* scores, int B, int K, int Lq,
+                         int Ld, int d, int32_t* status, void* stream);
+
+/*
+ * Training backward from the forward's argmax (shared docs).
+ *   grad_Q[n,q,:] = sum_b g[n,b] * D[b, argmax[n,b,q], :]
+ *   grad_D[b,t,:] = sum_{(n,q): argmax[n,b,q]==t} g[n,b] * Q[n,q,:]
+ * grad_scores: fp32 [Nq, B]. grad_Q: fp16 [Nq, Lq, d], grad_D: fp16
+ * [B, Ld, d]; both fully written (no pre-zeroing needed). Deterministic.
+ * Requires Nq * Lq <= 32768.
+ * Replaces `_maxsim_bwd_dQ_kernel` and `_maxsim_bwd_dD_kernel` launched by
+ *   _FlashMaxSimFn.backward (flash_maxsim/flash_maxsim.py:266-286,
+ *   kernels :153-188).
+ */
+int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
+                  const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
+                  int Lq, int Ld, int d, void* stream);
+
+/* element types accepted by fm_quantize_int8 */
+#define FM_DTYPE_F16 0
+#define FM_DTYPE_F32 1
+#define FM_DTYPE_BF16 2
+
+/*
+ * Per-token affine uint8 quantisation of `rows` rows of d elements
+ * (d % 8 == 0) of type `dtype` (FM_DTYPE_*), bit-exact with quantize_int8
+ * (flash_maxsim/flash_maxsim_quant.py:11-28): min/max in fp32,
+ * scale = max((max - min) / 255, 1e-8), u = clamp(round_half_even((x - min) / scale), 0, 255).
+ * Outputs: D_u8 [rows, d]; scales and mins fp16 [rows].
+ */
+int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,
+                     int64_t rows, int d, void* stream);
+
+/*
+ * Failure-detection self test: launches one CTA that waits on a barrier that
+ * nothing arrives at. The bounded wait gives up after timeout_ns and writes
+ * FM_ERR_TIMEOUT_SELFTEST into *status; the context stays usable.
+ * No counterpart in the reference (which has no device-side waits).
+ */
+int fm_wait_selftest(int32_t* status, int64_t timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_MAXSIM_SM100_H */
