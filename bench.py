@@ -1,0 +1,492 @@
+"""MaxSim scoring benchmark on B200 (one process per GPU; torchrun for N > 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+Default workload ("c2"): batched shared-docs scoring,
+Q [100, 32, 128] fp16 against D [100000, 300, 128] fp16 (7.68 GB), docs
+sharded across ranks (strong scaling: the 100000 docs are split N ways) and
+the per-rank score blocks combined with one NCCL all-gather. Inputs are
+synthetic: N(0, 1) entries, every token row L2-normalised, seeded per rank.
+
+A step = one pass of the hot path over the whole batch: the fused sm_100a
+MaxSim kernel on every rank, then the all-gather. Inputs (7.68 GB) exceed the
+126 MB L2, so no flush is needed between steps (configs whose inputs fit in L2
+flush it with a 512 MB write). `value` is query-doc scores per second of the
+whole job, device-timed with CUDA events, max over ranks. `e2e` repeats the
+step through the public API from pinned host buffers: host->device copy of Q
+and the rank's document shard, the kernel, the all-gather, and the
+device->host copy of the scores, all inside the timed region.
+
+`--impl reference` times the reference algorithm on the host CPU instead
+(the numpy restatement of the reference's maxsim_naive in oracle/, every host
+thread), on a bounded sample of the same workload per step; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "docs scored/sec per B200 and 8-GPU box; % of HBM or tensor-core roofline"
+L2_BYTES = 126 * 1024 * 1024
+
+# name: (description, Nq, Lq, B, Ld, d, kind)
+CONFIGS = {
+    "c1": ("textual single-query MaxSim Q[32,128] x D[1000,300,128] fp16", 1, 32, 1000, 300, 128, "single"),
+    "c2": ("batched shared-docs MaxSim Q[100,32,128] x D[100000,300,128] fp16, doc-sharded",
+           100, 32, 100000, 300, 128, "batched"),
+    "c3": ("visual late-interaction Q[16,1024,128] x D[4000,1024,128] fp16", 16, 1024, 4000, 1024, 128,
+           "batched"),
+    "c4": ("INT8 fused-dequant MaxSim Q[32,128] x u8 D[200000,300,128] + scale/min", 1, 32, 200000, 300,
+           128, "int8"),
+    "c5": ("varlen train fwd+bwd Q[64,64,256] x D[4096,1024,256], lengths U[32,1024]", 64, 64, 4096, 1024,
+           256, "train"),
+}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return {"hbm_gbs": j["hbm_gbs"], "tflops": j["bf16_tflops"],
+                "tflops_sustained": j.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic(cfg: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get(cfg)
+    return None
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, torch.device("cuda", torch.cuda.current_device())
+
+
+def physical_gpu_index(local: int) -> int:
+    """nvidia-smi index of CUDA device `local` (honours CUDA_VISIBLE_DEVICES)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if vis:
+        parts = [p.strip() for p in vis.split(",") if p.strip()]
+        if local < len(parts) and parts[local].isdigit():
+            return int(parts[local])
+    return local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs
+# ---------------------------------------------------------------------------
+
+def synth(shape, seed: int, device, chunk_rows: int = 4096) -> torch.Tensor:
+    """N(0, 1) entries, last-axis rows L2-normalised, fp16, built in chunks."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = torch.empty(shape, dtype=torch.float16, device=device)
+    flat = out.view(-1, shape[-1])
+    rows = flat.shape[0]
+    step = max(1, chunk_rows * 300)
+    for r0 in range(0, rows, step):
+        n = min(step, rows - r0)
+        x = torch.randn(n, shape[-1], generator=g, device=device, dtype=torch.float32)
+        flat[r0:r0 + n] = F.normalize(x, dim=-1).half()
+    return out
+
+
+def shard(B: int, rank: int, world: int):
+    lo = B * rank // world
+    hi = B * (rank + 1) // world
+    return lo, hi
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+
+def run_ours(args, cfg):
+    import flash_maxsim_b200 as fm
+    from flash_maxsim_b200 import sharded
+
+    desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
+    if args.docs:
+        # smaller document count, for ncu captures (same per-doc shapes)
+        B = args.docs
+        desc += f" [B overridden to {B}]"
+    rank, world, dev = dist_setup(args.gpus)
+    lo, hi = shard(B, rank, world)
+    Bl = hi - lo
+    peaks = load_peaks()
+    torch.manual_seed(0)
+
+    Q = synth((Nq, Lq, d) if kind != "single" and kind != "int8" else (Lq, d), 1, dev)
+    D = synth((Bl, Ld, d), 1000 + rank, dev)
+    lengths = None
+    if kind == "train":
+        gl = torch.Generator(device=dev).manual_seed(77 + rank)
+        lengths = torch.randint(32, Ld + 1, (Bl,), generator=gl, device=dev, dtype=torch.int32)
+    Du8 = sc = mn = None
+    if kind == "int8":
+        Du8, sc, mn = fm.quantize_int8(D)
+        del D
+        D = None
+        torch.cuda.empty_cache()
+    grad = None
+    if kind == "train":
+        grad = torch.randn(Nq, Bl, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+
+    in_bytes = (Du8.numel() + sc.numel() * 2 + mn.numel() * 2) if kind == "int8" else D.numel() * 2
+    flush = None
+    if in_bytes < 4 * L2_BYTES:
+        flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    stream = torch.cuda.current_stream(dev)
+
+    def kernel_step():
+        """The hot path once; returns (result, kernel start/end events)."""
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if kind == "single":
+            out = fm.flash_maxsim(Q, D)
+        elif kind == "batched":
+            out = fm.flash_maxsim_batched(Q, D)
+        elif kind == "int8":
+            out = fm.flash_maxsim_int8(Q, Du8, sc, mn)
+        else:
+            Qg = Q.detach().requires_grad_(True)
+            Dg = D.detach().requires_grad_(True)
+            s = fm.flash_maxsim_train(Qg, Dg, lengths)
+            s.backward(grad)
+            out = s.detach()
+        e1.record(stream)
+        return out, (e0, e1)
+
+    def step():
+        if flush is not None:
+            flush.fill_(1.0)
+        out, ev = kernel_step()
+        if world > 1:
+            out = sharded.all_gather_scores(out if out.dim() == 2 else out.unsqueeze(0), B)
+        return out, ev
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    fm.check_status(dev)
+
+    sampler = ClockSampler(physical_gpu_index(dev.index))
+    sampler.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    evs = []
+    t0.record(stream)
+    for _ in range(args.steps):
+        _, ev = step()
+        evs.append(ev)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    fm.check_status(dev)
+    total_ms = max_over_ranks(t0.elapsed_time(t1), world, dev)
+    kern_ms = [a.elapsed_time(b) for a, b in evs]
+    kern_avg_ms = max_over_ranks(sum(kern_ms) / len(kern_ms), world, dev)
+
+    units_total = (Nq * B) if kind in ("batched", "train") else B
+    unit_name = "query-doc scores/s" if kind in ("batched", "train") else "docs/s"
+    value = units_total / (total_ms / 1e3 / args.steps)
+
+    # roofline of the dominant kernel (per rank, per launch)
+    units_rank = (Nq * Bl) if kind in ("batched", "train") else Bl
+    flops = 2.0 * Nq * Lq * Ld * d * Bl
+    if kind == "train":
+        flops = 2.0 * Nq * Lq * float(lengths.sum().item()) * d
+    if kind in ("single", "int8"):
+        alg_bytes = in_bytes + Q.numel() * 2 + Bl * 4
+        achieved = alg_bytes / (kern_avg_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                "algorithmic_bytes_per_launch": alg_bytes}
+    else:
+        achieved = flops / (kern_avg_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["tflops"], 4),
+                "peak_source": peaks["source"] + " (burst bf16 cuBLAS; fp16 dense taken equal)",
+                "algorithmic_flops_per_launch": flops,
+                "hbm_achieved_GBs": round(in_bytes / (kern_avg_ms / 1e3) / 1e9, 1)}
+    tr = load_traffic(cfg)
+    roof["traffic"] = tr.get("bytes_per_launch") if tr else None
+    if tr:
+        roof["traffic_source"] = tr.get("source")
+    roof["kernel_ms"] = round(kern_avg_ms, 4)
+
+    # end to end through the public API from pinned host memory
+    e2e = None if args.no_e2e else run_e2e(args, kind, fm, sharded, Q, D, Du8, sc, mn, lengths, grad,
+                                           B, Bl, world, dev, units_total, unit_name)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(cfg, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": unit_name, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "strong",
+            "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic N(0,1), rows L2-normalised, seeded",
+            "config": {"workload": desc, "config": cfg, "Nq": Nq, "Lq": Lq, "B": B, "Ld": Ld, "d": d,
+                       "docs_per_rank": Bl, "parallelism": f"doc-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2" if flush is None else "L2 flushed (512 MB write) between steps"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps * (3 if kind == "train" else 1),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_e2e(args, kind, fm, sharded, Q, D, Du8, sc, mn, lengths, grad, B, Bl, world, dev,
+            units_total, unit_name):
+    """Same step through the public API, inputs from pinned host buffers."""
+    steps = max(2, min(args.steps, args.e2e_steps))
+    hQ = Q.cpu().pin_memory()
+    if kind == "int8":
+        hD = [Du8.cpu().pin_memory(), sc.cpu().pin_memory(), mn.cpu().pin_memory()]
+        dD = [torch.empty_like(Du8), torch.empty_like(sc), torch.empty_like(mn)]
+    else:
+        hD = [D.cpu().pin_memory()]
+        dD = [torch.empty_like(D)]
+    hL = lengths.cpu().pin_memory() if lengths is not None else None
+    h2d = hQ.numel() * hQ.element_size() + sum(t.numel() * t.element_size() for t in hD)
+    if hL is not None:
+        h2d += hL.numel() * 4
+    out_host = None
+    d2h = 0
+
+    def one():
+        nonlocal out_host, d2h
+        q = hQ.to(dev, non_blocking=True)
+        for h, dd in zip(hD, dD):
+            dd.copy_(h, non_blocking=True)
+        ln = hL.to(dev, non_blocking=True) if hL is not None else None
+        if kind == "single":
+            out = fm.flash_maxsim(q, dD[0])
+        elif kind == "batched":
+            out = fm.flash_maxsim_batched(q, dD[0])
+        elif kind == "int8":
+            out = fm.flash_maxsim_int8(q, dD[0], dD[1], dD[2])
+        else:
+            qg = q.requires_grad_(True)
+            dg = dD[0].requires_grad_(True)
+            s = fm.flash_maxsim_train(qg, dg, ln)
+            s.backward(grad)
+            out = s.detach()
+            dD[0] = dg.detach()
+        if world > 1:
+            out = sharded.all_gather_scores(out if out.dim() == 2 else out.unsqueeze(0), B)
+        if out_host is None:
+            out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            d2h = out.numel() * out.element_size()
+        out_host.copy_(out, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        one()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(a.elapsed_time(b), world, dev) / steps
+    return {"value": round(units_total / (ms / 1e3), 1), "unit": unit_name,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "ms_per_step": round(ms, 3)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference algorithm on the host cores)
+# ---------------------------------------------------------------------------
+
+def _cpu_sample_inputs(cfg: str, n_docs: int):
+    from oracle import maxsim_oracle as O
+    desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
+    nq = 1 if kind in ("single", "int8") else min(Nq, 4)
+    Q, D = O.seeded_inputs(123, (nq, Lq, d), (n_docs, Ld, d))
+    return O, Q, D, nq, kind
+
+
+def cpu_baseline(cfg: str, seconds: float):
+    """Reference maxsim (numpy port of maxsim_naive) on a bounded sample of the
+    workload, with every host thread; returns units per second."""
+    desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
+    n_docs = 256
+    O, Q, D, nq, kind = _cpu_sample_inputs(cfg, n_docs)
+    if kind == "int8":
+        u8, s, m = O.quantize_int8(D)
+        D = O.dequantize_int8(u8, s, m)
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        for n in range(nq):
+            O.maxsim(Q[n], D)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    units = done * n_docs * (nq if kind in ("batched", "train") else 1)
+    threads = os.environ.get("OMP_NUM_THREADS") or str(os.cpu_count())
+    unit_name = "query-doc scores/s" if kind in ("batched", "train") else "docs/s"
+    return {"value": round(units / el, 1), "unit": unit_name, "cores": int(threads), "kind": "port",
+            "sample": f"{nq} queries x {n_docs} docs of the {cfg} shapes, repeated for {el:.1f} s "
+                      "(numpy fp32 restatement of maxsim_naive, oracle/maxsim_oracle.py)"}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
+    per_step = max(0.5, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, per_step / 2)
+    vals = [cpu_baseline(cfg, per_step) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    base = vals[0]
+    line = {
+        "metric": METRIC, "impl": "reference", "value": v, "unit": base["unit"], "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), rows L2-normalised, seeded",
+        "ms_per_step": round(per_step * 1e3, 1),
+        "config": {"workload": desc, "config": cfg, "Nq": Nq, "Lq": Lq, "B": B, "Ld": Ld, "d": d},
+        "cpu_baseline": {"value": v, "unit": base["unit"], "cores": base["cores"], "kind": "port",
+                         "sample": base["sample"]},
+        "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--docs", type=int, default=0, help="override B (profiling captures)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args, args.config)
+    else:
+        run_ours(args, args.config)
+
+
+if __name__ == "__main__":
+    main()
