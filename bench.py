@@ -205,6 +205,11 @@ def run_ours(args, cfg):
         # smaller document count, for ncu captures (same per-doc shapes)
         B = args.docs
         desc += f" [B overridden to {B}]"
+    for name in ("nq", "lq", "ld", "dim"):
+        v = getattr(args, "shape_" + name)
+        if v:
+            Nq, Lq, Ld, d = [v if n == name else o for n, o in zip(("nq", "lq", "ld", "dim"), (Nq, Lq, Ld, d))]
+            desc += f" [{name} overridden to {v}]"
     rank, world, dev = dist_setup(args.gpus)
     lo, hi = shard(B, rank, world)
     Bl = hi - lo
@@ -478,6 +483,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    for name in ("nq", "lq", "ld", "dim"):
+        ap.add_argument(f"--shape-{name}", type=int, default=0, help="override a shape (tuning)")
     ap.add_argument("--docs", type=int, default=0, help="override B (profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -41,7 +41,7 @@ SIGNATURES = {
 }
 
 PLAN_FIELDS = ("C", "G", "nd", "nq", "nu", "nk", "kq_atoms", "d_atoms", "RS", "rep",
-               "q_resident", "nts", "ts_stride", "smem", "R")
+               "q_resident", "nts", "ts_stride", "smem", "R", "gd")
 
 
 def plan_info(mode: int, argmax: bool, Nq: int, B: int, Lq: int, Ld: int, d: int,

@@ -8,6 +8,8 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/flash_maxsim_sm100.h"
@@ -65,6 +67,35 @@ bool make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* 
   return r == CUDA_SUCCESS;
 }
 
+// Optional plan overrides for tuning sweeps, e.g.
+// FLASH_MAXSIM_TUNE="nd=3,nq=3,gd=2" (read once per process).
+struct Tune {
+  int nd = 0, nq = 0, G = 0, C = 0, dbg = 0, gd = 0;
+};
+const Tune& tune() {
+  static Tune t;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = std::getenv("FLASH_MAXSIM_TUNE");
+    if (!e) return;
+    const char* p = e;
+    while (*p) {
+      char key[8];
+      int v = 0, n = 0;
+      if (std::sscanf(p, "%7[a-zA-Z]=%d%n", key, &v, &n) != 2) break;
+      if (!std::strcmp(key, "nd")) t.nd = v;
+      if (!std::strcmp(key, "nq")) t.nq = v;
+      if (!std::strcmp(key, "G")) t.G = v;
+      if (!std::strcmp(key, "C")) t.C = v;
+      if (!std::strcmp(key, "dbg")) t.dbg = v;
+      if (!std::strcmp(key, "gd")) t.gd = v;
+      p += n;
+      if (*p == ',') ++p;
+    }
+  });
+  return t;
+}
+
 struct Shape {
   int mode;
   bool argmax;
@@ -72,8 +103,9 @@ struct Shape {
   int shared;
 };
 
-// Choose chunk size, ring depths and shared-memory carve-up.
-bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
+// Choose chunk size, ring depths and shared-memory carve-up for `gd`
+// documents per work item.
+bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
   const bool int8 = s.mode == MODE_INT8;
   a.Nq = s.Nq;
   a.B = s.B;
@@ -84,7 +116,8 @@ bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
   a.shared = s.shared;
   a.Gq = cdiv(s.Lq, 32);
   a.R = s.shared ? s.Nq * a.Gq : a.Gq;
-  a.n_work = s.shared ? s.B : s.Nq * s.B;
+  a.gd = gd;
+  a.n_work = s.shared ? cdiv(s.B, gd) : s.Nq * s.B;
   a.rep = a.R == 1 ? 4 : (a.R == 2 ? 2 : 1);
   const int atoms = cdiv(s.d, 64);
   a.kq_atoms = std::min(atoms, 2);
@@ -104,14 +137,17 @@ bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
     const int cap = (budget / (a.d_atoms * 128)) / 16 * 16;
     if (cap < 16) return false;
     a.C = std::min(a.C, cap);
+    if (tune().C >= 16 && tune().C % 16 == 0 && tune().C <= std::min(256, cap)) a.C = tune().C;
   }
   a.ts_stride = round_up(a.C, 32);
   a.nts = 512 / a.ts_stride;
   a.q_resident = (s.shared && a.R <= 4 && a.nk == 1) ? 1 : 0;
+  a.q_flat = (s.Lq % 32 == 0) ? 1 : 0;
+  a.dbg = tune().dbg;
   a.q_stage_bytes = a.kq_atoms * 16384u;
   a.d_slot_bytes = static_cast<uint32_t>(a.d_atoms) * a.C * 128u;
   a.u_slot_bytes = int8 ? static_cast<uint32_t>(a.d_atoms) * a.C * 64u : 0u;
-  a.rowbuf = (s.mode == MODE_SPARSE) ? a.Gq * 32 : a.R;
+  a.rowbuf = (s.mode == MODE_SPARSE) ? a.Gq * 32 : gd * a.R;
   const int nch_max = cdiv(s.Ld, a.C);
   const int mb_total = cdiv(a.R, 4);
 
@@ -120,13 +156,18 @@ bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
   const int qsum_bytes = int8 ? round_up(a.Gq * 32 * 4, 16) : 0;
   const int state_per_mb = 128 * 4 * (s.argmax ? 2 : 1);
 
-  for (int G = nch_max; G >= 1; --G) {
+  const int G_top = gd * nch_max;
+  for (int G = G_top; G >= 1; --G) {
+    if (gd > 1 && G != G_top) break;  // a document group is always fully resident
     if (a.nk > 1 && G > a.nts) continue;
+    if (tune().G > 0 && G != std::min(tune().G, nch_max)) continue;
     const bool multi = G < nch_max;
     const int nd_hi = a.q_resident && !int8 ? std::max(2 * G, 8) : 2 * G;
     for (int nd = nd_hi; nd >= G; --nd) {
+      if (tune().nd > 0 && nd != tune().nd) continue;
       const int nq_hi = a.q_resident ? 1 : 4, nq_lo = a.q_resident ? 1 : 2;
       for (int nq = nq_hi; nq >= nq_lo; --nq) {
+        if (tune().nq > 0 && !a.q_resident && nq != tune().nq) continue;
         const int nu_hi = int8 ? 6 : 0, nu_lo = int8 ? 2 : 0;
         for (int nu = nu_hi; nu >= nu_lo; --nu) {
           const int nbars = 2 * nq + 2 * nd + 2 * a.nts + 2 * nu + 1;
@@ -181,9 +222,27 @@ bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
   return false;
 }
 
+// Documents per work item: each streamed 128-row query block is used for
+// every chunk of an item, so short documents are grouped until an item holds
+// >= ~512 tokens (below that, delivering query blocks from L2 and the per
+// chunk hand-off, not the tensor core, limit the pass).  Falls back to
+// smaller groups when a group does not fit in shared memory.
+bool make_plan(const Shape& s, FwdArgs& a, int& smem_bytes) {
+  int gd = 1;
+  if (s.shared && s.mode == MODE_DENSE && s.Nq * cdiv(s.Lq, 32) > 2 && s.d <= 128) {
+    const int C0 = s.Ld <= 256 ? round_up(std::max(s.Ld, 16), 16)
+                               : round_up(cdiv(s.Ld, cdiv(s.Ld, 256)), 16);
+    gd = std::max(1, std::min(kMaxGroupDocs, cdiv(512, cdiv(s.Ld, C0) * C0)));
+  }
+  if (tune().gd > 0) gd = std::min(tune().gd, kMaxGroupDocs);
+  for (; gd >= 1; --gd)
+    if (plan_for_gd(s, gd, a, smem_bytes)) return true;
+  return false;
+}
+
 template <int MODE, bool ARGMAX>
-int launch_fwd(const CUtensorMap& tq, const CUtensorMap& td, const FwdArgs& a, int smem,
-               cudaStream_t stream) {
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tq2, const CUtensorMap& td, const FwdArgs& a,
+               int smem, cudaStream_t stream) {
   auto kern = maxsim_fwd_kernel<MODE, ARGMAX>;
   static std::atomic<int> configured_smem{0};
   if (configured_smem.load() < smem) {
@@ -196,7 +255,7 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& td, const FwdArgs& a, i
   if (sms <= 0) return FM_ERR_NO_DEVICE;
   const int grid = std::max(1, std::min(a.n_work, sms));
   const int threads = MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16;
-  kern<<<grid, threads, smem, stream>>>(tq, td, a);
+  kern<<<grid, threads, smem, stream>>>(tq, tq2, td, a);
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
@@ -227,9 +286,14 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   a.status = status;
   a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
 
-  CUtensorMap tq, td;
-  if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, s.mode == MODE_DENSE ? s.Nq : 1,
-                   64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+  CUtensorMap tq, tq2, td;
+  const int nq_rows = s.mode == MODE_DENSE ? s.Nq : 1;
+  if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, nq_rows, 64, 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  // the same rows as one [Nq * Lq, d] matrix, 128-row boxes
+  if (!make_map_3d(&tq2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d,
+                   static_cast<uint64_t>(s.Lq) * nq_rows, 1, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return FM_ERR_LAUNCH;
   if (s.mode == MODE_INT8) {
     if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, s.d, s.Ld, n_docs, 64, a.C,
@@ -242,12 +306,12 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   }
   switch (s.mode) {
     case MODE_DENSE:
-      return s.argmax ? launch_fwd<MODE_DENSE, true>(tq, td, a, smem, stream)
-                      : launch_fwd<MODE_DENSE, false>(tq, td, a, smem, stream);
+      return s.argmax ? launch_fwd<MODE_DENSE, true>(tq, tq2, td, a, smem, stream)
+                      : launch_fwd<MODE_DENSE, false>(tq, tq2, td, a, smem, stream);
     case MODE_SPARSE:
-      return launch_fwd<MODE_SPARSE, false>(tq, td, a, smem, stream);
+      return launch_fwd<MODE_SPARSE, false>(tq, tq2, td, a, smem, stream);
     case MODE_INT8:
-      return launch_fwd<MODE_INT8, false>(tq, td, a, smem, stream);
+      return launch_fwd<MODE_INT8, false>(tq, tq2, td, a, smem, stream);
   }
   return FM_ERR_ARG;
 }
@@ -287,15 +351,15 @@ void fm_set_wait_timeout_ns(int64_t ns) { g_timeout_ns.store(ns > 0 ? ns : 20000
 
 int fm_fwd_plan_info(int mode, int argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
                      int K, int32_t* out, int n_out) {
-  if (!out || n_out < 15 || mode < 0 || mode > 2) return FM_ERR_ARG;
+  if (!out || n_out < 16 || mode < 0 || mode > 2) return FM_ERR_ARG;
   if (Nq < 1 || B < 0 || Lq < 1 || Ld < 1 || d < 8 || d > 2048) return FM_ERR_ARG;
   Shape s{mode, argmax != 0, Nq, B, Lq, Ld, d, K, shared_docs ? 1 : 0};
   FwdArgs a{};
   int smem = 0;
   if (!make_plan(s, a, smem)) return FM_ERR_UNSUPPORTED;
-  const int32_t v[15] = {a.C, a.G, a.nd, a.nq, a.nu, a.nk, a.kq_atoms, a.d_atoms, a.RS, a.rep,
-                         a.q_resident, a.nts, a.ts_stride, smem, a.R};
-  for (int i = 0; i < 15; ++i) out[i] = v[i];
+  const int32_t v[16] = {a.C, a.G, a.nd, a.nq, a.nu, a.nk, a.kq_atoms, a.d_atoms, a.RS, a.rep,
+                         a.q_resident, a.nts, a.ts_stride, smem, a.R, a.gd};
+  for (int i = 0; i < 16; ++i) out[i] = v[i];
   return FM_OK;
 }
 
@@ -383,6 +447,19 @@ int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, 
   }
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
+
+#ifdef FM_PROFILE
+// profiling builds only: copy (and optionally clear) the wait/section counters
+int fm_prof_read(unsigned long long* out, int reset) {
+  if (cudaMemcpyFromSymbol(out, g_fm_prof, sizeof(unsigned long long) * 32) != cudaSuccess)
+    return FM_ERR_LAUNCH;
+  if (reset) {
+    const unsigned long long z[32] = {0};
+    if (cudaMemcpyToSymbol(g_fm_prof, z, sizeof(z)) != cudaSuccess) return FM_ERR_LAUNCH;
+  }
+  return FM_OK;
+}
+#endif
 
 int fm_wait_selftest(int32_t* status, int64_t timeout_ns, void* stream) {
   if (!status || timeout_ns <= 0) return FM_ERR_ARG;

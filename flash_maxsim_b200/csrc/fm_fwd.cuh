@@ -7,15 +7,18 @@
 // (flash_maxsim/flash_maxsim_quant.py:52-98) and its sparse variant
 // (flash_maxsim/flash_maxsim_sparse.py:42-91), organised for Blackwell:
 //
-//  * Work item = one document (shared docs: scored against every query;
-//    per-query docs: one (query, doc) pair).  Persistent CTAs stride over
-//    work items.
+//  * Work item = one document, or a group of up to kMaxGroupDocs consecutive
+//    documents when every document of the group fits in shared memory at
+//    once (shared docs).  Persistent CTAs stride over work items.
 //  * A document is split into chunks of C tokens (C <= 256, multiple of 16).
-//    A group of G chunks is kept resident in a shared-memory ring (D ring,
-//    filled by TMA from HBM, 128-byte swizzle, OOB rows zero-filled).
+//    The chunks of an item (or of one chunk group of a long document) stay
+//    resident in a shared-memory ring (D ring, filled by TMA from HBM,
+//    128-byte swizzle, OOB rows zero-filled).
 //  * Query rows are packed into 128-row "M-blocks" of four 32-row row groups
 //    (one row group = 32 consecutive tokens of one query, rows past Lq are
-//    TMA zero-fill).  M-blocks stream from L2 through a Q ring.
+//    TMA zero-fill).  M-blocks stream from L2 through a Q ring, and each one
+//    is used for every resident chunk of the item before it is released, so
+//    grouping short documents cuts the L2 -> SM query traffic per flop.
 //  * tcgen05.mma (M=128, N=C, K=16, fp16 in, fp32 accumulate) computes
 //    S = Qblock . Dchunk^T straight into TMEM: lane = query row,
 //    column = doc token.  TMEM holds a ring of accumulator slots, so the
@@ -29,6 +32,9 @@
 //    the row groups are replicated across the four TMEM lane quarters and the
 //    four epilogue warps split the columns between them, so the epilogue
 //    never limits an HBM-bound stream.
+//  * The single MMA-issuing thread does as little bookkeeping as possible:
+//    ring positions advance incrementally (no division), descriptors are a
+//    base plus constant offsets, and per-item state is scalar.
 //
 // Warp roles: 0 = D producer (TMA), 1 = MMA issuer + TMEM owner,
 // 2..5 = epilogue, 6 = Q producer (TMA), 7..10 = INT8 converters (INT8 only).
@@ -48,6 +54,7 @@ constexpr int kQProdWarp = 6;
 constexpr int kConvWarp0 = 7;
 constexpr int kThreadsF16 = 7 * 32;
 constexpr int kThreadsI8 = 11 * 32;
+constexpr int kMaxGroupDocs = 8;
 
 struct FwdArgs {
   const int32_t* lengths;    // [n_docs] valid tokens per doc, or null (all Ld)
@@ -61,11 +68,12 @@ struct FwdArgs {
   uint64_t timeout_ns;
   int Nq, B, Lq, Ld, d, K;
   int shared;                // 1: every doc against every query
+  int gd;                    // documents per work item (shared dense docs)
   int n_work;                // number of work items
   int Gq;                    // row groups per query = ceil(Lq / 32)
-  int R;                     // row groups per work item
+  int R;                     // row groups per document
   int C;                     // tokens per chunk (MMA N)
-  int G;                     // chunks per resident group
+  int G;                     // chunk slots of one resident group
   int nd;                    // D ring slots (chunks)
   int nq;                    // Q ring stages
   int nu;                    // INT8 staging slots
@@ -76,52 +84,85 @@ struct FwdArgs {
   int RS;                    // row groups per span when a doc needs >1 group
   int rep;                   // lane-quarter replication (1, 2 or 4)
   int q_resident;            // Q loaded once for the whole launch
+  int q_flat;                // Lq % 32 == 0: an M-block is 128 consecutive rows of Q
+  int dbg;                   // tuning experiments only: bit 0 skip epilogue reads, bit 1 skip MMAs
   int nts;                   // TMEM accumulator slots
   int ts_stride;             // TMEM columns per slot
-  int rowbuf;                // floats in the per-doc row buffer
+  int rowbuf;                // floats in the per-item row buffer
   uint32_t off_q, off_d, off_u, off_state, off_rows, off_xch, off_qsum, off_bar;
   uint32_t q_stage_bytes, d_slot_bytes, u_slot_bytes;
 };
 
-// Schedule of one work item, computed identically by every role.
+// Position in a ring of n slots: slot index and the parity of the current lap.
+struct Ring {
+  int idx = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+__device__ __forceinline__ int doc_len(const FwdArgs& a, int doc) {
+  int len = a.lengths ? __ldg(a.lengths + doc) : a.Ld;
+  return len < 0 ? 0 : (len > a.Ld ? a.Ld : len);
+}
+
+// Schedule of one work item, computed identically by every role.  Scalar
+// fields only; per-document lengths of a group are re-read when needed.
 struct Item {
-  int doc;      // index of the doc in D (flattened for per-query docs)
-  int b;        // score column
-  int n_lo;     // first query of the item
-  int nqi;      // queries in the item
-  int rg_lo;    // first row group
-  int rg_hi;    // one past the last row group
-  int len;      // valid tokens (clamped to [0, Ld])
-  int nch;      // chunks
-  int ngr;      // chunk groups
-  int span;     // row groups per span
+  int d0;        // first document (index into D, flattened for per-query docs)
+  int b0;        // score column of the first document
+  int ndocs;     // documents in the item (consecutive)
+  int len0;      // valid tokens of the first document
+  int nch0;      // chunks of the first document
+  int nch_total; // chunks of the whole item
+  int n_lo;      // first query of the item
+  int nqi;       // queries of the item
+  int rg_lo;     // first row group
+  int rg_hi;     // one past the last row group
+  int ngr;       // chunk groups (> 1 only for one long document)
+  int span;      // row groups per span
 };
 
 __device__ __forceinline__ Item make_item(const FwdArgs& a, int w) {
   Item it;
   if (a.shared) {
-    it.doc = w;
-    it.b = w;
+    it.d0 = w * a.gd;
+    it.b0 = it.d0;
+    it.ndocs = min(a.gd, a.B - it.d0);
     it.n_lo = 0;
     it.nqi = a.Nq;
     it.rg_lo = 0;
     it.rg_hi = a.Nq * a.Gq;
   } else {
     const int n = w / a.B;
-    it.doc = w;
-    it.b = w - n * a.B;
+    it.d0 = w;
+    it.b0 = w - n * a.B;
+    it.ndocs = 1;
     it.n_lo = n;
     it.nqi = 1;
     it.rg_lo = n * a.Gq;
     it.rg_hi = it.rg_lo + a.Gq;
   }
-  int len = a.lengths ? __ldg(a.lengths + it.doc) : a.Ld;
-  len = len < 0 ? 0 : (len > a.Ld ? a.Ld : len);
-  it.len = len;
-  it.nch = (len + a.C - 1) / a.C;
-  it.ngr = (it.nch + a.G - 1) / a.G;
+  it.len0 = doc_len(a, it.d0);
+  it.nch0 = (it.len0 + a.C - 1) / a.C;
+  it.nch_total = it.nch0;
+  for (int i = 1; i < it.ndocs; ++i) it.nch_total += (doc_len(a, it.d0 + i) + a.C - 1) / a.C;
+  if (it.ndocs == 1) {
+    it.ngr = (it.nch0 + a.G - 1) / a.G;
+  } else {
+    it.ngr = it.nch_total > 0 ? 1 : 0;
+  }
   it.span = (it.ngr > 1) ? a.RS : (it.rg_hi - it.rg_lo);
   return it;
+}
+
+// Chunks of chunk group g (a long single document is split in groups of G).
+__device__ __forceinline__ int group_chunks(const FwdArgs& a, const Item& it, int g) {
+  return it.ndocs == 1 ? min(a.G, it.nch0 - g * a.G) : it.nch_total;
 }
 
 // M-blocks in a span of row groups [s0, s1)
@@ -207,10 +248,77 @@ __device__ __forceinline__ void piece_max(const float (&v)[32], int nv, int col0
   }
 }
 
+// One 32-column piece in the epilogue: INT8 affine map (scale * acc +
+// min * rowsum(q)) if needed, then the running max.
+template <int MODE, bool ARGMAX>
+__device__ __forceinline__ void epi_piece(float (&v)[32], int nv, int col0, const FwdArgs& a, int b,
+                                          float qsum, int lane, RowAcc<ARGMAX>& acc) {
+  if (MODE == MODE_INT8) {
+    const size_t tb = static_cast<size_t>(b) * a.Ld + col0;
+    const int col = lane < nv ? lane : 0;
+    const float sc = __half2float(a.scales[tb + col]);
+    const float mn = __half2float(a.mins[tb + col]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float s_i = __shfl_sync(0xffffffffu, sc, i);
+      const float m_i = __shfl_sync(0xffffffffu, mn, i);
+      v[i] = fmaf(s_i, v[i], m_i * qsum);
+    }
+  }
+  piece_max<ARGMAX>(v, nv, col0, acc);
+}
+
+// Row max over the first `valid` columns of one accumulator slot, plain fp16
+// scoring (no argmax, no INT8 map): full 32-column pieces two per TMEM wait,
+// then the ragged tail masked with -inf.  Compact on purpose: the epilogue
+// runs one warp per scheduler, so its instruction count sets its speed.
+__device__ __forceinline__ void chunk_max_plain(uint32_t taddr, int valid, RowAcc<false>& acc) {
+  const int nfull = valid >> 5;
+  int q = 0;
+  for (; q + 2 <= nfull; q += 2) {
+    float v0[32], v1[32];
+    tmem_ld32(taddr + q * 32, v0);
+    tmem_ld32(taddr + q * 32 + 32, v1);
+    tmem_wait_ld();
+    piece_max<false>(v0, 32, 0, acc);
+    piece_max<false>(v1, 32, 0, acc);
+  }
+  const int rem = valid - q * 32;  // 0..63 columns left
+  if (rem > 0) {
+    float v0[32];
+    tmem_ld32(taddr + q * 32, v0);
+    tmem_wait_ld();
+    if (rem < 32) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v0[i] = i < rem ? v0[i] : -INFINITY;
+    }
+    piece_max<false>(v0, 32, 0, acc);
+    if (rem > 32) {
+      tmem_ld32(taddr + q * 32 + 32, v0);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v0[i] = i < rem - 32 ? v0[i] : -INFINITY;
+      piece_max<false>(v0, 32, 0, acc);
+    }
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
+}
+
+// Bounded wait for the last phase of `bar` used by a ring position (drain
+// before exit); records FM_ERR_TIMEOUT_DRAIN when it gives up.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, const FwdArgs& a) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > a.timeout_ns) {
+      record_status(a.status, FM_ERR_TIMEOUT_DRAIN);
+      break;
+    }
+  }
 }
 
 // -------------------------------------------------------------------------
@@ -219,6 +327,7 @@ __device__ __forceinline__ float warp_sum(float x) {
 template <int MODE, bool ARGMAX>
 __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 1)
     maxsim_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                      const __grid_constant__ CUtensorMap tmap_q2,
                       const __grid_constant__ CUtensorMap tmap_d, const FwdArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment of the operand rings (required by the 128 B swizzle)
@@ -267,6 +376,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_q2);
     tma_prefetch_desc(&tmap_d);
   }
   // Zero the Q ring and the K-padding atoms of every D slot once: padded
@@ -291,210 +401,256 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
 
   const int w0 = blockIdx.x;
   const int wstep = gridDim.x;
+  FM_PROF_T0(pk0);
 
   if (warp == 0) {
     // ===================== D producer =====================
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      int dcnt = 0;
+      const int nslots = (MODE == MODE_INT8) ? a.nu : a.nd;
+      const uint32_t tx = a.d_atoms_real * a.C * ((MODE == MODE_INT8) ? 64u : 128u);
+      const uint32_t slot_bytes = (MODE == MODE_INT8) ? a.u_slot_bytes : a.d_slot_bytes;
+      const uint32_t atom_bytes = a.C * ((MODE == MODE_INT8) ? 64u : 128u);
+      const uint32_t ring_base = sbase + ((MODE == MODE_INT8) ? a.off_u : a.off_d);
+      Ring r;
+      int issued = 0;
       bool ok = true;
       for (int w = w0; w < a.n_work && ok; w += wstep) {
         const Item it = make_item(a, w);
         for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
           for (int g = 0; g < it.ngr && ok; ++g) {
-            const int c0 = g * a.G;
-            const int cn = min(a.G, it.nch - c0);
-            for (int c = 0; c < cn; ++c) {
-              if (MODE == MODE_INT8) {
-                const int slot = dcnt % a.nu;
-                const uint32_t ph = (dcnt / a.nu) & 1;
-                if (!mbar_wait(bars.u_empty(slot), ph ^ 1, ctl, FM_ERR_TIMEOUT_UEMPTY)) { ok = false; break; }
-                mbar_expect_tx(bars.u_full(slot), a.d_atoms_real * a.C * 64u);
-                const uint32_t dst = sbase + a.off_u + slot * a.u_slot_bytes;
-                for (int at = 0; at < a.d_atoms_real; ++at)
-                  tma_load_3d(dst + at * a.C * 64, &tmap_d, at * 64, (c0 + c) * a.C, it.doc,
-                              bars.u_full(slot), pol);
+            for (int i = 0; i < it.ndocs && ok; ++i) {
+              const int doc = it.d0 + i;
+              int cb = 0, ce;
+              if (it.ndocs == 1) {
+                cb = g * a.G;
+                ce = min(it.nch0, cb + a.G);
               } else {
-                const int slot = dcnt % a.nd;
-                const uint32_t ph = (dcnt / a.nd) & 1;
-                if (!mbar_wait(bars.d_empty(slot), ph ^ 1, ctl, FM_ERR_TIMEOUT_DEMPTY)) { ok = false; break; }
-                mbar_expect_tx(bars.d_full(slot), a.d_atoms_real * a.C * 128u);
-                const uint32_t dst = sbase + a.off_d + slot * a.d_slot_bytes;
-                for (int at = 0; at < a.d_atoms_real; ++at)
-                  tma_load_3d(dst + at * a.C * 128, &tmap_d, at * 64, (c0 + c) * a.C, it.doc,
-                              bars.d_full(slot), pol);
+                ce = (doc_len(a, doc) + a.C - 1) / a.C;
               }
-              ++dcnt;
+              for (int c = cb; c < ce; ++c) {
+                const uint32_t empty = (MODE == MODE_INT8) ? bars.u_empty(r.idx) : bars.d_empty(r.idx);
+                const uint32_t full = (MODE == MODE_INT8) ? bars.u_full(r.idx) : bars.d_full(r.idx);
+                if (!mbar_wait(empty, r.phase ^ 1u, ctl,
+                               MODE == MODE_INT8 ? FM_ERR_TIMEOUT_UEMPTY : FM_ERR_TIMEOUT_DEMPTY)) {
+                  ok = false;
+                  break;
+                }
+                mbar_expect_tx(full, tx);
+                const uint32_t dst = ring_base + r.idx * slot_bytes;
+                for (int at = 0; at < a.d_atoms_real; ++at)
+                  tma_load_3d(dst + at * atom_bytes, &tmap_d, at * 64, c * a.C, doc, full, pol);
+                r.next(nslots);
+                ++issued;
+              }
             }
           }
         }
       }
       // Wait (bounded) for the last load issued into every slot to land so
       // no bulk copy is in flight when the CTA exits.
-      const int nslots = (MODE == MODE_INT8) ? a.nu : a.nd;
-      for (int i = 0; i < nslots && i < dcnt; ++i) {
-        const int k = dcnt - 1 - i;
-        const int slot = (MODE == MODE_INT8) ? k % a.nu : k % a.nd;
-        const uint32_t ph = (MODE == MODE_INT8) ? (k / a.nu) & 1 : (k / a.nd) & 1;
-        const uint32_t bar = (MODE == MODE_INT8) ? bars.u_full(slot) : bars.d_full(slot);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(bar, ph)) {
-          if (globaltimer_ns() - t0 > a.timeout_ns) {
-            record_status(a.status, FM_ERR_TIMEOUT_DRAIN);
-            break;
-          }
+      for (int i = 0; i < nslots && i < issued; ++i) {
+        if (--r.idx < 0) {
+          r.idx = nslots - 1;
+          r.phase ^= 1u;
         }
+        drain_wait((MODE == MODE_INT8) ? bars.u_full(r.idx) : bars.d_full(r.idx), r.phase, a);
       }
     }
   } else if (warp == kQProdWarp) {
     // ===================== Q producer =====================
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_last();
-      int qcnt = 0;
+      Ring r;
+      int issued = 0;
       bool ok = true;
       for (int w = w0; w < a.n_work && ok; w += wstep) {
         const Item it = make_item(a, w);
-        if (it.nch == 0) continue;
+        if (it.nch_total == 0) continue;
         for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
           const int s1 = min(it.rg_hi, s0 + it.span);
           const int nmb = span_mblocks(a, s0, s1);
           for (int g = 0; g < it.ngr && ok; ++g) {
             for (int jb = 0; jb < nmb && ok; ++jb) {
               for (int ks = 0; ks < a.nk; ++ks) {
-                if (a.q_resident && qcnt > 0) break;
-                const int slot = qcnt % a.nq;
-                const uint32_t ph = (qcnt / a.nq) & 1;
-                if (!mbar_wait(bars.q_empty(slot), ph ^ 1, ctl, FM_ERR_TIMEOUT_QEMPTY)) { ok = false; break; }
-                int nload = 0;
-                for (int sub = 0; sub < 4; ++sub) {
-                  const int rg = (a.rep > 1) ? s0 + sub / a.rep : s0 + 4 * jb + sub;
-                  if (rg < s1) ++nload;
+                if (a.q_resident && issued > 0) break;
+                if (!mbar_wait(bars.q_empty(r.idx), r.phase ^ 1u, ctl, FM_ERR_TIMEOUT_QEMPTY)) {
+                  ok = false;
+                  break;
                 }
                 const int at_hi = min(a.kq_atoms, a.d_atoms_real - ks * a.kq_atoms);
-                mbar_expect_tx(bars.q_full(slot), nload * at_hi * 4096u);
-                const uint32_t dst = sbase + a.off_q + slot * a.q_stage_bytes;
-                for (int sub = 0; sub < 4; ++sub) {
-                  const int rg = (a.rep > 1) ? s0 + sub / a.rep : s0 + 4 * jb + sub;
-                  if (rg >= s1) continue;
-                  const int qn = rg / a.Gq;
-                  const int qy = (rg - qn * a.Gq) * 32;
+                const uint32_t dst = sbase + a.off_q + r.idx * a.q_stage_bytes;
+                const uint32_t full = bars.q_full(r.idx);
+                if (a.q_flat && a.rep == 1) {
+                  // one 128-row box per K atom (rows past the span are loaded but unused)
+                  mbar_expect_tx(full, at_hi * 16384u);
                   for (int at = 0; at < at_hi; ++at)
-                    tma_load_3d(dst + at * 16384 + sub * 4096, &tmap_q, (ks * a.kq_atoms + at) * 64,
-                                qy, qn, bars.q_full(slot), pol);
+                    tma_load_3d(dst + at * 16384, &tmap_q2, (ks * a.kq_atoms + at) * 64,
+                                (s0 + 4 * jb) * 32, 0, full, pol);
+                } else {
+                  int nload = 0;
+                  for (int sub = 0; sub < 4; ++sub) {
+                    const int rg = (a.rep > 1) ? s0 + sub / a.rep : s0 + 4 * jb + sub;
+                    if (rg < s1) ++nload;
+                  }
+                  mbar_expect_tx(full, nload * at_hi * 4096u);
+                  for (int sub = 0; sub < 4; ++sub) {
+                    const int rg = (a.rep > 1) ? s0 + sub / a.rep : s0 + 4 * jb + sub;
+                    if (rg >= s1) continue;
+                    const int qn = rg / a.Gq;
+                    const int qy = (rg - qn * a.Gq) * 32;
+                    for (int at = 0; at < at_hi; ++at)
+                      tma_load_3d(dst + at * 16384 + sub * 4096, &tmap_q, (ks * a.kq_atoms + at) * 64,
+                                  qy, qn, full, pol);
+                  }
                 }
-                ++qcnt;
+                r.next(a.nq);
+                ++issued;
               }
             }
           }
         }
       }
-      for (int i = 0; i < a.nq && i < qcnt; ++i) {
-        const int k = qcnt - 1 - i;
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(bars.q_full(k % a.nq), (k / a.nq) & 1)) {
-          if (globaltimer_ns() - t0 > a.timeout_ns) {
-            record_status(a.status, FM_ERR_TIMEOUT_DRAIN);
-            break;
-          }
+      for (int i = 0; i < a.nq && i < issued; ++i) {
+        if (--r.idx < 0) {
+          r.idx = a.nq - 1;
+          r.phase ^= 1u;
         }
+        drain_wait(bars.q_full(r.idx), r.phase, a);
       }
     }
   } else if (warp == 1) {
     // ===================== MMA issuer =====================
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(128, a.C);
-      const int ksteps = a.kq_atoms * 4;  // K=16 steps per Q stage
-      int dcnt = 0, qcnt = 0, tcnt = 0;
+      const int ksteps = a.kq_atoms * 4;  // K=16 steps per Q stage (4 or 8)
+      const uint32_t b_atom = a.C * 8u;    // one K atom of a D slot, in 16-byte units
+      const bool skip_mma = (a.dbg & 2) != 0;
+      Ring dr, qr, tr;
       bool ok = true;
       for (int w = w0; w < a.n_work && ok; w += wstep) {
         const Item it = make_item(a, w);
-        if (it.nch == 0) continue;
+        if (it.nch_total == 0) continue;
         for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
           const int s1 = min(it.rg_hi, s0 + it.span);
           const int nmb = span_mblocks(a, s0, s1);
           for (int g = 0; g < it.ngr && ok; ++g) {
-            const int c0 = g * a.G;
-            const int cn = min(a.G, it.nch - c0);
-            for (int c = 0; c < cn && ok; ++c) {
-              const int k = dcnt + c;
-              if (!mbar_wait(bars.d_full(k % a.nd), (k / a.nd) & 1, ctl, FM_ERR_TIMEOUT_DFULL)) ok = false;
+            const int cn = group_chunks(a, it, g);
+            {
+              Ring r = dr;
+              for (int c = 0; c < cn; ++c) {
+                if (!mbar_wait(bars.d_full(r.idx), r.phase, ctl, FM_ERR_TIMEOUT_DFULL)) {
+                  ok = false;
+                  break;
+                }
+                r.next(a.nd);
+              }
             }
             if (!ok) break;
             tc_fence_after();
             for (int jb = 0; jb < nmb && ok; ++jb) {
               if (a.nk == 1) {
-                const int qslot = a.q_resident ? 0 : qcnt % a.nq;
-                const uint32_t qph = a.q_resident ? 0 : (qcnt / a.nq) & 1;
-                if (!mbar_wait(bars.q_full(qslot), qph, ctl, FM_ERR_TIMEOUT_QFULL)) { ok = false; break; }
+                const int qslot = a.q_resident ? 0 : qr.idx;
+                const uint32_t qph = a.q_resident ? 0u : qr.phase;
+                if (!mbar_wait(bars.q_full(qslot), qph, ctl, FM_ERR_TIMEOUT_QFULL)) {
+                  ok = false;
+                  break;
+                }
                 tc_fence_after();
-                const uint32_t qaddr = sbase + a.off_q + qslot * a.q_stage_bytes;
+                const uint64_t adesc = smem_desc_sw128(sbase + a.off_q + qslot * a.q_stage_bytes);
+                Ring r = dr;
                 for (int c = 0; c < cn; ++c) {
-                  const int ts = tcnt % a.nts;
-                  if (!mbar_wait(bars.t_empty(ts), ((tcnt / a.nts) & 1) ^ 1, ctl, FM_ERR_TIMEOUT_TEMPTY)) { ok = false; break; }
-                  tc_fence_after();
-                  const uint32_t daddr = sbase + a.off_d + ((dcnt + c) % a.nd) * a.d_slot_bytes;
-                  const uint32_t tacc = tmem_base + ts * a.ts_stride;
-                  for (int kk = 0; kk < ksteps; ++kk) {
-                    const int at = kk >> 2, sub = kk & 3;
-                    const uint64_t adesc = smem_desc_sw128(qaddr + at * 16384 + sub * 32);
-                    const uint64_t bdesc = smem_desc_sw128(daddr + at * a.C * 128 + sub * 32);
-                    tc_mma_f16(tacc, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
+                  if (!mbar_wait(bars.t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
+                    ok = false;
+                    break;
                   }
-                  tc_commit(bars.t_full(ts));
-                  ++tcnt;
+                  tc_fence_after();
+                  const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes);
+                  const uint32_t tacc = tmem_base + tr.idx * a.ts_stride;
+                  FM_PROF_T0(pm0);
+                  if (!skip_mma) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                      if (kk < ksteps) {
+                        // +32 bytes per K=16 step inside a 128-byte atom, next atom after 4
+                        const uint64_t ao = (kk >> 2) * (16384u >> 4) + (kk & 3) * 2u;
+                        const uint64_t bo = (kk >> 2) * b_atom + (kk & 3) * 2u;
+                        tc_mma_f16(tacc, adesc + ao, bdesc + bo, idesc, kk > 0 ? 1u : 0u);
+                      }
+                    }
+                  }
+                  FM_PROF_ADD(20, pm0);
+                  tc_commit(bars.t_full(tr.idx));
+                  tr.next(a.nts);
+                  r.next(a.nd);
                 }
                 if (!ok) break;
-                if (!a.q_resident) tc_commit(bars.q_empty(qslot));
-                ++qcnt;
+                if (!a.q_resident) {
+                  tc_commit(bars.q_empty(qr.idx));
+                  qr.next(a.nq);
+                }
               } else {
-                // K split over several Q stages: every chunk slot of this
-                // M-block stays live until the last stage.
-                for (int c = 0; c < cn && ok; ++c) {
-                  const int t = tcnt + c;
-                  if (!mbar_wait(bars.t_empty(t % a.nts), ((t / a.nts) & 1) ^ 1, ctl, FM_ERR_TIMEOUT_TEMPTY)) ok = false;
+                // K split over several Q stages (single-document items only):
+                // every chunk slot of this M-block stays live until the last stage.
+                {
+                  Ring t = tr;
+                  for (int c = 0; c < cn; ++c) {
+                    if (!mbar_wait(bars.t_empty(t.idx), t.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
+                      ok = false;
+                      break;
+                    }
+                    t.next(a.nts);
+                  }
                 }
                 if (!ok) break;
                 tc_fence_after();
                 for (int ks = 0; ks < a.nk && ok; ++ks) {
-                  const int qslot = qcnt % a.nq;
-                  if (!mbar_wait(bars.q_full(qslot), (qcnt / a.nq) & 1, ctl, FM_ERR_TIMEOUT_QFULL)) { ok = false; break; }
-                  tc_fence_after();
-                  const uint32_t qaddr = sbase + a.off_q + qslot * a.q_stage_bytes;
-                  for (int c = 0; c < cn; ++c) {
-                    const uint32_t daddr = sbase + a.off_d + ((dcnt + c) % a.nd) * a.d_slot_bytes;
-                    const uint32_t tacc = tmem_base + ((tcnt + c) % a.nts) * a.ts_stride;
-                    for (int kk = 0; kk < ksteps; ++kk) {
-                      const int at = kk >> 2, sub = kk & 3;
-                      const uint64_t adesc = smem_desc_sw128(qaddr + at * 16384 + sub * 32);
-                      const uint64_t bdesc =
-                          smem_desc_sw128(daddr + (ks * a.kq_atoms + at) * a.C * 128 + sub * 32);
-                      tc_mma_f16(tacc, adesc, bdesc, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-                    }
+                  if (!mbar_wait(bars.q_full(qr.idx), qr.phase, ctl, FM_ERR_TIMEOUT_QFULL)) {
+                    ok = false;
+                    break;
                   }
-                  tc_commit(bars.q_empty(qslot));
-                  ++qcnt;
+                  tc_fence_after();
+                  const uint64_t adesc = smem_desc_sw128(sbase + a.off_q + qr.idx * a.q_stage_bytes);
+                  Ring r = dr, t = tr;
+                  for (int c = 0; c < cn; ++c) {
+                    const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes) +
+                                           ks * a.kq_atoms * b_atom;
+                    const uint32_t tacc = tmem_base + t.idx * a.ts_stride;
+                    if (!skip_mma) {
+#pragma unroll
+                      for (int kk = 0; kk < 8; ++kk) {
+                        if (kk < ksteps) {
+                          const uint64_t ao = (kk >> 2) * (16384u >> 4) + (kk & 3) * 2u;
+                          const uint64_t bo = (kk >> 2) * b_atom + (kk & 3) * 2u;
+                          tc_mma_f16(tacc, adesc + ao, bdesc + bo, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+                        }
+                      }
+                    }
+                    r.next(a.nd);
+                    t.next(a.nts);
+                  }
+                  tc_commit(bars.q_empty(qr.idx));
+                  qr.next(a.nq);
                 }
                 if (!ok) break;
-                for (int c = 0; c < cn; ++c) tc_commit(bars.t_full((tcnt + c) % a.nts));
-                tcnt += cn;
+                for (int c = 0; c < cn; ++c) {
+                  tc_commit(bars.t_full(tr.idx));
+                  tr.next(a.nts);
+                }
               }
             }
             if (!ok) break;
-            for (int c = 0; c < cn; ++c) tc_commit(bars.d_empty((dcnt + c) % a.nd));
-            dcnt += cn;
+            for (int c = 0; c < cn; ++c) {
+              tc_commit(bars.d_empty(dr.idx));
+              dr.next(a.nd);
+            }
           }
         }
       }
       // make sure every MMA issued by this thread has completed before the
       // TMEM is released
       tc_commit(bars.drain());
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(bars.drain(), 0)) {
-        if (globaltimer_ns() - t0 > a.timeout_ns) {
-          record_status(a.status, FM_ERR_TIMEOUT_DRAIN);
-          break;
-        }
-      }
+      drain_wait(bars.drain(), 0, a);
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ===================== epilogue =====================
@@ -509,6 +665,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
     const int rep = a.rep;
     const int part = sub % rep;
     const int ppc = (a.C + 31) / 32;  // 32-column pieces per chunk
+    const bool skip_epi = (a.dbg & 1) != 0;
 
     float* qsum_s = reinterpret_cast<float*>(smem + a.off_qsum);
     if (MODE == MODE_INT8) {
@@ -523,23 +680,26 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       }
       named_bar_sync(1, 128);
     }
-    int tcnt = 0;
+    Ring tr;
     bool ok = true;
     for (int w = w0; w < a.n_work && ok; w += wstep) {
       const Item it = make_item(a, w);
-      if (it.nch == 0) {
-        // empty document: every query row has max = -inf
-        if (MODE == MODE_DENSE) {
-          for (int i = et; i < it.nqi; i += 128)
-            a.scores[static_cast<size_t>(it.n_lo + i) * a.B + it.b] = -INFINITY;
-        } else if (et == 0) {
-          a.scores[it.b] = (MODE == MODE_SPARSE && a.K == 0) ? 0.f : -INFINITY;
-        }
-        if (ARGMAX) {
-          for (int i = et; i < it.nqi * a.Lq; i += 128) {
-            const int n = it.n_lo + i / a.Lq;
-            const int q = i - (i / a.Lq) * a.Lq;
-            a.argmax[(static_cast<size_t>(n) * a.B + it.b) * a.Lq + q] = -1;
+      if (it.nch_total == 0) {
+        // only empty documents: every query row has max = -inf
+        for (int i = 0; i < it.ndocs; ++i) {
+          const int b = it.b0 + i;
+          if (MODE == MODE_DENSE) {
+            for (int n = et; n < it.nqi; n += 128)
+              a.scores[static_cast<size_t>(it.n_lo + n) * a.B + b] = -INFINITY;
+          } else if (et == 0) {
+            a.scores[b] = (MODE == MODE_SPARSE && a.K == 0) ? 0.f : -INFINITY;
+          }
+          if (ARGMAX) {
+            for (int e = et; e < it.nqi * a.Lq; e += 128) {
+              const int n = it.n_lo + e / a.Lq;
+              const int q = e - (e / a.Lq) * a.Lq;
+              a.argmax[(static_cast<size_t>(n) * a.B + b) * a.Lq + q] = -1;
+            }
           }
         }
         continue;
@@ -548,99 +708,119 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         const int s1 = min(it.rg_hi, s0 + it.span);
         const int nmb = span_mblocks(a, s0, s1);
         for (int g = 0; g < it.ngr && ok; ++g) {
-          const int c0 = g * a.G;
-          const int cn = min(a.G, it.nch - c0);
           for (int jb = 0; jb < nmb && ok; ++jb) {
             const int rg = (rep > 1) ? s0 + sub / rep : s0 + 4 * jb + sub;
             const bool active = rg < s1;
             const int qrow = (rg % a.Gq) * 32 + lane;
             const float qsum = (MODE == MODE_INT8 && active) ? qsum_s[qrow] : 0.f;
-            RowAcc<ARGMAX> acc;
-            acc.init();
-            for (int c = 0; c < cn; ++c) {
-              const int ts = tcnt % a.nts;
-              if (!mbar_wait(bars.t_full(ts), (tcnt / a.nts) & 1, ctl, FM_ERR_TIMEOUT_TFULL)) { ok = false; break; }
-              tc_fence_after();
-              if (active) {
-                const int tok0 = (c0 + c) * a.C;
-                const int valid = min(a.C, it.len - tok0);
-                const int npieces = (valid + 31) >> 5;
-                const uint32_t taddr = tmem_base + lane_base + ts * a.ts_stride;
-                // piece p of this chunk belongs to part ((c*ppc + p) % rep)
-                int p = 0;
-                if (rep > 1) {
-                  const int first = (c * ppc) % rep;
-                  p = (part - first + rep) % rep;
-                }
-                for (; p < npieces; p += rep) {
-                  float v[32];
-                  tmem_ld32(taddr + p * 32, v);
-                  tmem_wait_ld();
-                  const int nv = min(32, valid - p * 32);
-                  if (MODE == MODE_INT8) {
-                    const size_t tb = static_cast<size_t>(it.b) * a.Ld + tok0 + p * 32;
-                    const int col = lane < nv ? lane : 0;
-                    const float sc = __half2float(a.scales[tb + col]);
-                    const float mn = __half2float(a.mins[tb + col]);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                      const float s_i = __shfl_sync(0xffffffffu, sc, i);
-                      const float m_i = __shfl_sync(0xffffffffu, mn, i);
-                      v[i] = fmaf(s_i, v[i], m_i * qsum);
-                    }
-                  }
-                  piece_max<ARGMAX>(v, nv, tok0 + p * 32, acc);
-                }
-              }
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(bars.t_empty(ts));
-              ++tcnt;
-            }
-            if (!ok) break;
-            // combine across chunk groups
-            if (it.ngr > 1) {
-              const int si = jb * 128 + sub * 32 + lane;
-              if (g == 0) {
-                state_m[si] = acc.m;
-                if (ARGMAX) state_i[si] = acc.idx;
+            for (int i = 0; i < it.ndocs && ok; ++i) {
+              int cb = 0, ce, len;
+              if (it.ndocs == 1) {
+                cb = g * a.G;
+                ce = min(it.nch0, cb + a.G);
+                len = it.len0;
               } else {
-                RowAcc<ARGMAX> prev;
-                prev.m = state_m[si];
-                prev.idx = ARGMAX ? state_i[si] : 0;
-                prev.merge(acc.m, acc.idx);
-                acc = prev;
-                if (g < it.ngr - 1) {
+                len = doc_len(a, it.d0 + i);
+                ce = (len + a.C - 1) / a.C;
+              }
+              const int b = it.b0 + i;
+              RowAcc<ARGMAX> acc;
+              acc.init();
+              for (int c = cb; c < ce; ++c) {
+                if (!mbar_wait(bars.t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                FM_PROF_T0(pe0);
+                if (MODE != MODE_INT8 && !ARGMAX && rep == 1) {
+                  if (active && !skip_epi)
+                    chunk_max_plain(tmem_base + lane_base + tr.idx * a.ts_stride,
+                                    min(a.C, len - c * a.C), *reinterpret_cast<RowAcc<false>*>(&acc));
+                } else if (active && !skip_epi) {
+                  const int tok0 = c * a.C;
+                  const int valid = min(a.C, len - tok0);
+                  const int npieces = (valid + 31) >> 5;
+                  const uint32_t taddr = tmem_base + lane_base + tr.idx * a.ts_stride;
+                  // piece p of this chunk belongs to part ((c * ppc + p) % rep)
+                  int p = 0;
+                  if (rep > 1) {
+                    const int first = (c * ppc) % rep;
+                    p = (part - first + rep) % rep;
+                  }
+                  // two TMEM loads in flight per wait
+                  for (; p < npieces; p += 2 * rep) {
+                    const int p1 = p + rep;
+                    const bool two = p1 < npieces;
+                    float v0[32], v1[32];
+
+                    tmem_ld32(taddr + p * 32, v0);
+                    if (two) tmem_ld32(taddr + p1 * 32, v1);
+                    tmem_wait_ld();
+
+                    epi_piece<MODE, ARGMAX>(v0, min(32, valid - p * 32), tok0 + p * 32, a, b, qsum,
+                                            lane, acc);
+                    if (two)
+                      epi_piece<MODE, ARGMAX>(v1, min(32, valid - p1 * 32), tok0 + p1 * 32, a, b,
+                                              qsum, lane, acc);
+                  }
+                }
+                FM_PROF_ADD(22 + sub, pe0);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bars.t_empty(tr.idx));
+                tr.next(a.nts);
+              }
+              if (!ok) break;
+              FM_PROF_T0(pf0);
+              // combine across chunk groups (single-document items)
+              if (it.ngr > 1) {
+                const int si = jb * 128 + sub * 32 + lane;
+                if (g == 0) {
                   state_m[si] = acc.m;
                   if (ARGMAX) state_i[si] = acc.idx;
-                }
-              }
-            }
-            if (g == it.ngr - 1) {
-              if (rep > 1) {
-                xch_m[sub * 32 + lane] = acc.m;
-                if (ARGMAX) xch_i[sub * 32 + lane] = acc.idx;
-              } else {
-                const bool rv = active && qrow < a.Lq;
-                if (MODE == MODE_SPARSE) {
-                  if (rv) rows[qrow] = acc.m;
                 } else {
-                  const float tot = warp_sum(rv ? acc.m : 0.f);
-                  if (lane == 0 && active) rows[rg - it.rg_lo] = tot;
-                }
-                if (ARGMAX && rv) {
-                  const int n = rg / a.Gq;
-                  a.argmax[(static_cast<size_t>(n) * a.B + it.b) * a.Lq + qrow] = acc.idx;
+                  RowAcc<ARGMAX> prev;
+                  prev.m = state_m[si];
+                  prev.idx = ARGMAX ? state_i[si] : 0;
+                  prev.merge(acc.m, acc.idx);
+                  acc = prev;
+                  if (g < it.ngr - 1) {
+                    state_m[si] = acc.m;
+                    if (ARGMAX) state_i[si] = acc.idx;
+                  }
                 }
               }
+              if (g == it.ngr - 1) {
+                if (rep > 1) {
+                  xch_m[sub * 32 + lane] = acc.m;
+                  if (ARGMAX) xch_i[sub * 32 + lane] = acc.idx;
+                } else {
+                  const bool rv = active && qrow < a.Lq;
+                  if (MODE == MODE_SPARSE) {
+                    if (rv) rows[qrow] = acc.m;
+                  } else {
+                    const float tot = warp_sum(rv ? acc.m : 0.f);
+                    if (lane == 0 && active) rows[i * a.R + rg - it.rg_lo] = tot;
+                  }
+                  if (ARGMAX && rv) {
+                    const int n = rg / a.Gq;
+                    a.argmax[(static_cast<size_t>(n) * a.B + b) * a.Lq + qrow] = ce > 0 ? acc.idx : -1;
+                  }
+                }
+              }
+              FM_PROF_ADD(28, pf0);
             }
           }
         }
       }
       if (!ok) break;
-      // ---- per-doc finalisation (epilogue warps only) ----
+      // ---- per-item finalisation (epilogue warps only) ----
+      FM_PROF_T0(pi0);
       named_bar_sync(1, 128);
+      FM_PROF_ADD(29, pi0);
       if (rep > 1) {
+        // single-document items: combine the column parts of each row
         if (part == 0) {
           RowAcc<ARGMAX> acc;
           acc.m = xch_m[sub * 32 + lane];
@@ -658,7 +838,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
           }
           if (ARGMAX && rv) {
             const int n = rg / a.Gq;
-            a.argmax[(static_cast<size_t>(n) * a.B + it.b) * a.Lq + qrow] = acc.idx;
+            a.argmax[(static_cast<size_t>(n) * a.B + it.b0) * a.Lq + qrow] = acc.idx;
           }
         }
         named_bar_sync(1, 128);
@@ -667,7 +847,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         // score = sum_k rowmax[idx[b, k]] in a fixed order
         if (warp == kEpiWarp0) {
           float s = 0.f;
-          const int32_t* ip = a.sp_idx + static_cast<size_t>(it.b) * a.K;
+          const int32_t* ip = a.sp_idx + static_cast<size_t>(it.b0) * a.K;
           for (int k = lane; k < a.K; k += 32) {
             int q = __ldg(ip + k);
             if (q < 0) q += a.Lq;
@@ -678,16 +858,21 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
             s += rows[q];
           }
           s = warp_sum(s);
-          if (lane == 0) a.scores[it.b] = s;
+          if (lane == 0) a.scores[it.b0] = s;
         }
       } else {
-        for (int i = et; i < it.nqi; i += 128) {
+        for (int e = et; e < it.ndocs * it.nqi; e += 128) {
+          const int i = e / it.nqi;
+          const int n = e - i * it.nqi;
           float s = 0.f;
-          for (int gq = 0; gq < a.Gq; ++gq) s += rows[i * a.Gq + gq];
-          a.scores[static_cast<size_t>(it.n_lo + i) * a.B + it.b] = s;
+          for (int gq = 0; gq < a.Gq; ++gq) s += rows[i * a.R + n * a.Gq + gq];
+          a.scores[static_cast<size_t>(it.n_lo + n) * a.B + it.b0 + i] = s;
         }
       }
+      FM_PROF_T0(pi1);
       named_bar_sync(1, 128);
+      FM_PROF_ADD(30, pi1);
+      FM_PROF_ADD(31, pi0);
     }
   } else if (MODE == MODE_INT8 && warp >= kConvWarp0 && warp < kConvWarp0 + 4) {
     // ===================== INT8 converters =====================
@@ -696,7 +881,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
     // (0x6400 | u is the fp16 value 1024 + u; subtracting 1024 leaves u);
     // the per-token affine map scale * u + min is applied in the epilogue.
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
-    int ucnt = 0;
+    Ring ur, dr;
     bool ok = true;
     const int n16 = a.d_atoms_real * a.C * 4;  // 16-byte pieces of one u8 chunk
     const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
@@ -704,14 +889,12 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       const Item it = make_item(a, w);
       for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
         for (int g = 0; g < it.ngr && ok; ++g) {
-          const int cn = min(a.G, it.nch - g * a.G);
+          const int cn = group_chunks(a, it, g);
           for (int c = 0; c < cn; ++c) {
-            const int uslot = ucnt % a.nu;
-            const int dslot = ucnt % a.nd;
-            if (!mbar_wait(bars.u_full(uslot), (ucnt / a.nu) & 1, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
-            if (!mbar_wait(bars.d_empty(dslot), ((ucnt / a.nd) & 1) ^ 1, ctl, FM_ERR_TIMEOUT_DEMPTY)) { ok = false; break; }
-            const uint8_t* src = smem + a.off_u + uslot * a.u_slot_bytes;
-            uint8_t* dst = smem + a.off_d + dslot * a.d_slot_bytes;
+            if (!mbar_wait(bars.u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
+            if (!mbar_wait(bars.d_empty(dr.idx), dr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_DEMPTY)) { ok = false; break; }
+            const uint8_t* src = smem + a.off_u + ur.idx * a.u_slot_bytes;
+            uint8_t* dst = smem + a.off_d + dr.idx * a.d_slot_bytes;
             for (int i = ct; i < n16; i += 128) {
               const int at = i / (a.C * 4);
               const int rem = i - at * (a.C * 4);
@@ -736,15 +919,17 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
               *reinterpret_cast<uint4*>(rowp + j1 * 16) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
             }
             fence_proxy_async_smem();
-            mbar_arrive(bars.d_full(dslot));
-            mbar_arrive(bars.u_empty(uslot));
-            ++ucnt;
+            mbar_arrive(bars.d_full(dr.idx));
+            mbar_arrive(bars.u_empty(ur.idx));
+            ur.next(a.nu);
+            dr.next(a.nd);
           }
         }
       }
     }
   }
 
+  if (threadIdx.x == 0) FM_PROF_ADD(27, pk0);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

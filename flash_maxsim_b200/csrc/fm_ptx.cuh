@@ -70,10 +70,28 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   atomicCAS(status, 0, code);
 }
 
+#ifdef FM_PROFILE
+// Profiling builds only (never shipped): cycles spent in each kind of wait
+// (indexed by its timeout code) and in a few named sections, summed over the
+// lane-0 threads of every CTA.
+__device__ unsigned long long g_fm_prof[32];
+#define FM_PROF_T0(v) const long long v = clock64()
+#define FM_PROF_ADD(code, t0)                                                                  \
+  do {                                                                                         \
+    if ((threadIdx.x & 31) == 0)                                                               \
+      atomicAdd(&g_fm_prof[code], static_cast<unsigned long long>(clock64() - (t0)));          \
+  } while (0)
+#else
+#define FM_PROF_T0(v)
+#define FM_PROF_ADD(code, t0) \
+  do {                        \
+  } while (0)
+#endif
+
 // Bounded wait on an mbarrier phase. Returns false when the CTA is aborting
 // (this wait ran out of time, or another role's did).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
-                                          int code) {
+__device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
+                                               int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -85,6 +103,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
+                                          int code) {
+#ifdef FM_PROFILE
+  FM_PROF_T0(c0);
+  const bool r = mbar_wait_impl(bar, parity, ctl, code);
+  FM_PROF_ADD(code & 31, c0);
+  return r;
+#else
+  return mbar_wait_impl(bar, parity, ctl, code);
+#endif
 }
 
 // ---------------------------------------------------------------------------

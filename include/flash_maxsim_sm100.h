@@ -56,12 +56,12 @@ void fm_set_wait_timeout_ns(int64_t ns);
 
 /*
  * Launch plan the forward entry points would use for a shape (host only, no
- * device needed). mode: 0 dense, 1 sparse, 2 INT8. Writes 15 ints to `out`:
+ * device needed). mode: 0 dense, 1 sparse, 2 INT8. Writes 16 ints to `out`:
  * chunk tokens C, chunks per resident group G, D ring slots, Q ring stages,
  * INT8 staging slots, Q stages per M-block, K atoms per Q stage, K atoms per
  * token, row groups per span, lane-quarter replication, Q resident flag, TMEM
  * slots, TMEM columns per slot, dynamic shared memory bytes, row groups per
- * work item. No counterpart in the reference (its Triton autotuner picks tile
+ * document, documents per work item. No counterpart in the reference (its Triton autotuner picks tile
  * sizes at run time, flash_maxsim/flash_maxsim.py:15-81).
  */
 int fm_fwd_plan_info(int mode, int argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
