@@ -134,7 +134,9 @@ bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
   }
   {
     const int budget = kMaxSmem - 2 * a.kq_atoms * 16384 - 16 * 1024;
-    const int cap = (budget / (a.d_atoms * 128)) / 16 * 16;
+    // fp16: one D slot per chunk; INT8: one fp16 slot plus two uint8 staging slots
+    const int per_token = a.d_atoms * (int8 ? 256 : 128);
+    const int cap = (budget / per_token) / 16 * 16;
     if (cap < 16) return false;
     a.C = std::min(a.C, cap);
     if (tune().C >= 16 && tune().C % 16 == 0 && tune().C <= std::min(256, cap)) a.C = tune().C;
