@@ -15,6 +15,7 @@
 #include "../../include/flash_maxsim_sm100.h"
 #include "fm_aux.cuh"
 #include "fm_fwd.cuh"
+#include "fm_int8.cuh"
 
 namespace fm {
 namespace {
@@ -164,19 +165,21 @@ bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
     if (a.nk > 1 && G > a.nts) continue;
     if (tune().G > 0 && G != std::min(tune().G, nch_max)) continue;
     const bool multi = G < nch_max;
-    const int nd_hi = a.q_resident && !int8 ? std::max(2 * G, 8) : 2 * G;
+    // INT8 keeps its read-ahead in the (half-size) uint8 staging ring instead
+    const int nd_hi = int8 ? G + 1 : (a.q_resident ? std::max(2 * G, 8) : 2 * G);
     for (int nd = nd_hi; nd >= G; --nd) {
       if (tune().nd > 0 && nd != tune().nd) continue;
       const int nq_hi = a.q_resident ? 1 : 4, nq_lo = a.q_resident ? 1 : 2;
       for (int nq = nq_hi; nq >= nq_lo; --nq) {
         if (tune().nq > 0 && !a.q_resident && nq != tune().nq) continue;
-        const int nu_hi = int8 ? 6 : 0, nu_lo = int8 ? 2 : 0;
+        const int nu_hi = int8 ? 8 : 0, nu_lo = int8 ? 2 : 0;
         for (int nu = nu_hi; nu >= nu_lo; --nu) {
-          const int nbars = 2 * nq + 2 * nd + 2 * a.nts + 2 * nu + 1;
+          const int nbars = 2 * nq + 2 * nd + 2 * a.nts + 2 * nu + (int8 ? nd : 0) + 1;
+          const int sc_bytes = int8 ? nd * a.C * 8 : 0;
           const int bar_bytes = round_up(nbars * 8 + 16, 16);
           const int base = 1024 + nq * static_cast<int>(a.q_stage_bytes) +
                            nd * static_cast<int>(a.d_slot_bytes) + nu * static_cast<int>(a.u_slot_bytes) +
-                           rows_bytes + xch_bytes + qsum_bytes + bar_bytes;
+                           sc_bytes + rows_bytes + xch_bytes + qsum_bytes + bar_bytes;
           if (base > kMaxSmem) continue;
           int state_bytes = 0;
           int RS;
@@ -205,6 +208,8 @@ bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
           off += nd * a.d_slot_bytes;
           a.off_u = off;
           off += nu * a.u_slot_bytes;
+          a.off_sc = off;
+          off += sc_bytes;
           a.off_state = off;
           off += state_bytes;
           a.off_rows = off;
@@ -318,6 +323,79 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   return FM_ERR_ARG;
 }
 
+// INT8 fast path: uint8 codes straight into kind::i8 MMAs (fm_int8.cuh).
+bool int8_fast_ok(int Lq, int d) { return Lq <= 64 && d >= 128 && d <= 256 && d % 16 == 0; }
+
+bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
+  a.B = B;
+  a.Lq = Lq;
+  a.Ld = Ld;
+  a.d = d;
+  const int gq = cdiv(Lq, 32);
+  a.N = 64 * gq;
+  a.nts = 512 / a.N;
+  a.atoms = cdiv(d, 128);
+  a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
+  a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);
+  const int q_bytes = a.atoms * a.N * 128;
+  const int misc = round_up((64 + 64 + kI8Xch * 4 * gq * 32) * 4 + 2 * kI8Xch * 4, 16);
+  const int per_slot = static_cast<int>(a.u_slot_bytes + a.sc_slot_bytes) + 16;
+  const int fixed = 1024 + round_up(q_bytes, 1024) + misc + (2 * a.nts + 2) * 8 + 32;
+  a.nu = std::min(16, (kMaxSmem - fixed) / per_slot);
+  if (tune().nd > 0) a.nu = std::min(a.nu, tune().nd);
+  if (a.nu < 2) return false;
+  uint32_t off = 0;
+  a.off_q = off;
+  off += round_up(q_bytes, 1024);
+  a.off_u = off;
+  off += a.nu * a.u_slot_bytes;
+  a.off_sc = off;
+  off += a.nu * a.sc_slot_bytes;
+  a.off_misc = round_up(off, 16);
+  off = a.off_misc + misc;
+  a.off_bar = round_up(off, 16);
+  off = a.off_bar + (2 * a.nu + 2 * a.nts + 2) * 8 + 32;
+  smem = std::max(static_cast<int>(off) + 1024, kMinSmem);
+  return smem <= kMaxSmem;
+}
+
+template <int GQ>
+int launch_int8_gq(const CUtensorMap& tu, const Int8Args& a, int smem, cudaStream_t stream) {
+  static std::atomic<bool> cfg{false};
+  if (!cfg.load()) {
+    if (cudaFuncSetAttribute(maxsim_int8_kernel<GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxSmem) != cudaSuccess)
+      return FM_ERR_LAUNCH;
+    cfg.store(true);
+  }
+  const int sms = sm_count();
+  if (sms <= 0) return FM_ERR_NO_DEVICE;
+  maxsim_int8_kernel<GQ><<<std::max(1, std::min(a.B, sms)), kThreadsI8Fast, smem, stream>>>(tu, a);
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int launch_int8_fast(const void* Q, const void* Du8, const void* scales, const void* mins,
+                     const int32_t* lengths, float* scores, int B, int Lq, int Ld, int d,
+                     int32_t* status, cudaStream_t stream) {
+  Int8Args a{};
+  int smem = 0;
+  if (!plan_int8_fast(B, Lq, Ld, d, a, smem)) return FM_ERR_UNSUPPORTED;
+  if (!aligned16(scales) || !aligned16(mins)) return FM_ERR_ARG;
+  a.lengths = lengths;
+  a.scores = scores;
+  a.q = static_cast<const __half*>(Q);
+  a.scales = static_cast<const __half*>(scales);
+  a.mins = static_cast<const __half*>(mins);
+  a.status = status;
+  a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
+  a.sc_total_bytes = static_cast<size_t>(B) * Ld * 2;
+  CUtensorMap tu;
+  if (!make_map_3d(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Du8, d, Ld, B, 128, kI8Tokens,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  return a.N == 64 ? launch_int8_gq<1>(tu, a, smem, stream) : launch_int8_gq<2>(tu, a, smem, stream);
+}
+
 }  // namespace
 }  // namespace fm
 
@@ -376,6 +454,14 @@ int fm_maxsim_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengt
 int fm_maxsim_int8_fwd(const uint16_t* Q, const uint8_t* D_u8, const uint16_t* scales,
                        const uint16_t* mins, const int32_t* doc_lengths, float* scores, int B,
                        int Lq, int Ld, int d, int32_t* status, void* stream) {
+  if (int8_fast_ok(Lq, d) && tune().dbg != 8) {
+    if (!Q || !D_u8 || !scales || !mins || !scores || !status || B < 0 || Ld < 1 || Lq < 1)
+      return FM_ERR_ARG;
+    if (!aligned16(Q) || !aligned16(D_u8)) return FM_ERR_ARG;
+    if (B == 0) return FM_OK;
+    return launch_int8_fast(Q, D_u8, scales, mins, doc_lengths, scores, B, Lq, Ld, d, status,
+                            static_cast<cudaStream_t>(stream));
+  }
   Shape s{MODE_INT8, false, 1, B, Lq, Ld, d, 0, 1};
   return fwd_common(s, Q, D_u8, doc_lengths, scores, nullptr, nullptr, scales, mins, status,
                     static_cast<cudaStream_t>(stream));

@@ -89,7 +89,7 @@ struct FwdArgs {
   int nts;                   // TMEM accumulator slots
   int ts_stride;             // TMEM columns per slot
   int rowbuf;                // floats in the per-item row buffer
-  uint32_t off_q, off_d, off_u, off_state, off_rows, off_xch, off_qsum, off_bar;
+  uint32_t off_q, off_d, off_u, off_sc, off_state, off_rows, off_xch, off_qsum, off_bar;
   uint32_t q_stage_bytes, d_slot_bytes, u_slot_bytes;
 };
 
@@ -183,7 +183,13 @@ struct SmemBars {
   __device__ uint32_t u_empty(int i) const {
     return base + 8u * (2 * nq + 2 * nd + 2 * nts + nu + i);
   }
-  __device__ uint32_t drain() const { return base + 8u * (2 * nq + 2 * nd + 2 * nts + 2 * nu); }
+  // INT8: per-token scale/min staging of D slot i released by the epilogue
+  __device__ uint32_t s_empty(int i) const {
+    return base + 8u * (2 * nq + 2 * nd + 2 * nts + 2 * nu + i);
+  }
+  __device__ uint32_t drain() const {
+    return base + 8u * (2 * nq + 2 * nd + 2 * nts + 2 * nu + (nu ? nd : 0));
+  }
   __device__ uint32_t end() const { return drain() + 8u; }
 };
 
@@ -249,20 +255,17 @@ __device__ __forceinline__ void piece_max(const float (&v)[32], int nv, int col0
 }
 
 // One 32-column piece in the epilogue: INT8 affine map (scale * acc +
-// min * rowsum(q)) if needed, then the running max.
+// min * rowsum(q), per-token scale/min staged in shared memory as float2 by
+// the converter warps; `sm` points at this piece's first column) if needed,
+// then the running max.
 template <int MODE, bool ARGMAX>
-__device__ __forceinline__ void epi_piece(float (&v)[32], int nv, int col0, const FwdArgs& a, int b,
-                                          float qsum, int lane, RowAcc<ARGMAX>& acc) {
+__device__ __forceinline__ void epi_piece(float (&v)[32], int nv, int col0, const float2* sm,
+                                          float qsum, RowAcc<ARGMAX>& acc) {
   if (MODE == MODE_INT8) {
-    const size_t tb = static_cast<size_t>(b) * a.Ld + col0;
-    const int col = lane < nv ? lane : 0;
-    const float sc = __half2float(a.scales[tb + col]);
-    const float mn = __half2float(a.mins[tb + col]);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float s_i = __shfl_sync(0xffffffffu, sc, i);
-      const float m_i = __shfl_sync(0xffffffffu, mn, i);
-      v[i] = fmaf(s_i, v[i], m_i * qsum);
+      const float2 sc = sm[i];
+      v[i] = fmaf(sc.x, v[i], sc.y * qsum);
     }
   }
   piece_max<ARGMAX>(v, nv, col0, acc);
@@ -365,6 +368,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         mbar_init(bars.u_full(i), 1);
         mbar_init(bars.u_empty(i), 128);
       }
+      for (int i = 0; i < a.nd; ++i) mbar_init(bars.s_empty(i), 4);
     }
     mbar_init(bars.drain(), 1);
     *abort_flag = 0;
@@ -680,7 +684,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       }
       named_bar_sync(1, 128);
     }
-    Ring tr;
+    Ring tr, er;
     bool ok = true;
     for (int w = w0; w < a.n_work && ok; w += wstep) {
       const Item it = make_item(a, w);
@@ -709,6 +713,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         const int nmb = span_mblocks(a, s0, s1);
         for (int g = 0; g < it.ngr && ok; ++g) {
           for (int jb = 0; jb < nmb && ok; ++jb) {
+            Ring sr = er;  // INT8: D-ring position of the group's first chunk
             const int rg = (rep > 1) ? s0 + sub / rep : s0 + 4 * jb + sub;
             const bool active = rg < s1;
             const int qrow = (rg % a.Gq) * 32 + lane;
@@ -727,6 +732,17 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
               RowAcc<ARGMAX> acc;
               acc.init();
               for (int c = cb; c < ce; ++c) {
+                const float2* scs = nullptr;
+                if (MODE == MODE_INT8) {
+                  // the slot's scales were written before its d_full arrival; the slot
+                  // cannot be refilled before this warp releases it (s_empty)
+                  if (!mbar_wait(bars.d_full(sr.idx), sr.phase, ctl, FM_ERR_TIMEOUT_DFULL)) {
+                    ok = false;
+                    break;
+                  }
+                  scs = reinterpret_cast<const float2*>(smem + a.off_sc) + sr.idx * a.C;
+                  sr.next(a.nd);
+                }
                 if (!mbar_wait(bars.t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) {
                   ok = false;
                   break;
@@ -758,11 +774,11 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     if (two) tmem_ld32(taddr + p1 * 32, v1);
                     tmem_wait_ld();
 
-                    epi_piece<MODE, ARGMAX>(v0, min(32, valid - p * 32), tok0 + p * 32, a, b, qsum,
-                                            lane, acc);
+                    epi_piece<MODE, ARGMAX>(v0, min(32, valid - p * 32), tok0 + p * 32, scs + p * 32,
+                                            qsum, acc);
                     if (two)
-                      epi_piece<MODE, ARGMAX>(v1, min(32, valid - p1 * 32), tok0 + p1 * 32, a, b,
-                                              qsum, lane, acc);
+                      epi_piece<MODE, ARGMAX>(v1, min(32, valid - p1 * 32), tok0 + p1 * 32, scs + p1 * 32,
+                                              qsum, acc);
                   }
                 }
                 FM_PROF_ADD(22 + sub, pe0);
@@ -810,6 +826,14 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 }
               }
               FM_PROF_ADD(28, pf0);
+            }
+          }
+          if (MODE == MODE_INT8 && ok) {
+            // release the group's scale staging (after its last M-block)
+            const int cn = group_chunks(a, it, g);
+            for (int c = 0; c < cn; ++c) {
+              if (lane == 0) mbar_arrive(bars.s_empty(er.idx));
+              er.next(a.nd);
             }
           }
         }
@@ -877,46 +901,68 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
   } else if (MODE == MODE_INT8 && warp >= kConvWarp0 && warp < kConvWarp0 + 4) {
     // ===================== INT8 converters =====================
     // uint8 staging slot (64-byte rows per 64-element atom, no swizzle) ->
-    // fp16 128-byte-swizzled operand slot.  u is converted exactly
-    // (0x6400 | u is the fp16 value 1024 + u; subtracting 1024 leaves u);
-    // the per-token affine map scale * u + min is applied in the epilogue.
+    // fp16 128-byte-swizzled operand slot holding 1024 + u (0x6400 | u, exact);
+    // the per-token affine map is applied in the epilogue.
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
     Ring ur, dr;
     bool ok = true;
-    const int n16 = a.d_atoms_real * a.C * 4;  // 16-byte pieces of one u8 chunk
-    const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
     for (int w = w0; w < a.n_work && ok; w += wstep) {
       const Item it = make_item(a, w);
       for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
         for (int g = 0; g < it.ngr && ok; ++g) {
-          const int cn = group_chunks(a, it, g);
-          for (int c = 0; c < cn; ++c) {
+          // single-document items (INT8 scores one query against each doc)
+          const int cb = g * a.G, ce = min(it.nch0, cb + a.G);
+          for (int c = cb; c < ce; ++c) {
             if (!mbar_wait(bars.u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
             if (!mbar_wait(bars.d_empty(dr.idx), dr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_DEMPTY)) { ok = false; break; }
+            if (!mbar_wait(bars.s_empty(dr.idx), dr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_DEMPTY)) { ok = false; break; }
             const uint8_t* src = smem + a.off_u + ur.idx * a.u_slot_bytes;
             uint8_t* dst = smem + a.off_d + dr.idx * a.d_slot_bytes;
-            for (int i = ct; i < n16; i += 128) {
-              const int at = i / (a.C * 4);
-              const int rem = i - at * (a.C * 4);
-              const int row = rem >> 2;
-              const int ch = rem & 3;
-              const uint4 u = *reinterpret_cast<const uint4*>(src + at * a.C * 64 + row * 64 + ch * 16);
-              uint32_t hv[8];
-              const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint32_t lo = __byte_perm(wds[j], 0x64646464u, 0x5140);
-                uint32_t hi = __byte_perm(wds[j], 0x64646464u, 0x7362);
-                __half2 hlo = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
-                __half2 hhi = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
-                hv[2 * j] = *reinterpret_cast<uint32_t*>(&hlo);
-                hv[2 * j + 1] = *reinterpret_cast<uint32_t*>(&hhi);
+            // per-token (scale, min - 1024 * scale) of this chunk as fp32 pairs: the
+            // operand holds 1024 + u (fp16 0x6400 | u, exact), so
+            // scale * <q, 1024 + u> + (min - 1024 * scale) * sum(q) = <q, scale * u + min>
+            float2* scs = reinterpret_cast<float2*>(smem + a.off_sc) + dr.idx * a.C;
+            const size_t tb = static_cast<size_t>(it.b0) * a.Ld + static_cast<size_t>(c) * a.C;
+            for (int t = ct; t < a.C; t += 128) {
+              float sv = 0.f, mv = 0.f;
+              if (c * a.C + t < it.len0) {
+                sv = __half2float(a.scales[tb + t]);
+                mv = __half2float(a.mins[tb + t]);
               }
-              uint8_t* rowp = dst + at * a.C * 128 + row * 128;
-              const int j0 = (2 * ch) ^ (row & 7);
-              const int j1 = (2 * ch + 1) ^ (row & 7);
-              *reinterpret_cast<uint4*>(rowp + j0 * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-              *reinterpret_cast<uint4*>(rowp + j1 * 16) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+              scs[t] = make_float2(sv, fmaf(-1024.f, sv, mv));
+            }
+            // lane -> (row, 16-byte column) of a 64-byte uint8 row; 32 rows per pass,
+            // four passes unrolled for independent shared-memory loads
+            const int ch = ct & 3;
+            const int r0 = ct >> 2;
+            for (int at = 0; at < a.d_atoms_real; ++at) {
+              const uint8_t* s_at = src + at * a.C * 64 + ch * 16;
+              uint8_t* d_at = dst + at * a.C * 128;
+              for (int rb = 0; rb < a.C; rb += 128) {
+                uint4 u[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const int row = rb + r0 + 32 * k;
+                  if (row < a.C) u[k] = *reinterpret_cast<const uint4*>(s_at + row * 64);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const int row = rb + r0 + 32 * k;
+                  if (row < a.C) {
+                    const uint32_t wds[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
+                    uint32_t hv[8];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                      hv[2 * j] = __byte_perm(wds[j], 0x64646464u, 0x5140);
+                      hv[2 * j + 1] = __byte_perm(wds[j], 0x64646464u, 0x7362);
+                    }
+                    uint8_t* rowp = d_at + row * 128;
+                    const int sw = row & 7;
+                    *reinterpret_cast<uint4*>(rowp + (((2 * ch) ^ sw) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                    *reinterpret_cast<uint4*>(rowp + (((2 * ch + 1) ^ sw) << 4)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+                  }
+                }
+              }
             }
             fence_proxy_async_smem();
             mbar_arrive(bars.d_full(dr.idx));
