@@ -333,12 +333,12 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   a.d = d;
   const int gq = cdiv(Lq, 32);
   a.N = 64 * gq;
-  a.nts = 512 / a.N;
+  a.nts = 512 / (2 * a.N);  // a slot holds the two 128-token halves of a chunk
   a.atoms = cdiv(d, 128);
   a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
   a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);
   const int q_bytes = a.atoms * a.N * 128;
-  const int misc = round_up((64 + 64 + kI8Xch * 4 * gq * 32) * 4 + 2 * kI8Xch * 4, 16);
+  const int misc = round_up((64 + 64 + kI8Xch * 8 * gq * 32) * 4 + 2 * kI8Xch * 4, 16);
   const int per_slot = static_cast<int>(a.u_slot_bytes + a.sc_slot_bytes) + 16;
   const int fixed = 1024 + round_up(q_bytes, 1024) + misc + (2 * a.nts + 2) * 8 + 32;
   a.nu = std::min(16, (kMaxSmem - fixed) / per_slot);
@@ -359,18 +359,18 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   return smem <= kMaxSmem;
 }
 
-template <int GQ>
+template <int GQ, int EW>
 int launch_int8_gq(const CUtensorMap& tu, const Int8Args& a, int smem, cudaStream_t stream) {
   static std::atomic<bool> cfg{false};
   if (!cfg.load()) {
-    if (cudaFuncSetAttribute(maxsim_int8_kernel<GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(maxsim_int8_kernel<GQ, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxSmem) != cudaSuccess)
       return FM_ERR_LAUNCH;
     cfg.store(true);
   }
   const int sms = sm_count();
   if (sms <= 0) return FM_ERR_NO_DEVICE;
-  maxsim_int8_kernel<GQ><<<std::max(1, std::min(a.B, sms)), kThreadsI8Fast, smem, stream>>>(tu, a);
+  maxsim_int8_kernel<GQ, EW><<<std::max(1, std::min(a.B, sms)), i8_threads(EW), smem, stream>>>(tu, a);
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
@@ -389,11 +389,13 @@ int launch_int8_fast(const void* Q, const void* Du8, const void* scales, const v
   a.status = status;
   a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
   a.sc_total_bytes = static_cast<size_t>(B) * Ld * 2;
+  a.dbg = tune().dbg;
   CUtensorMap tu;
   if (!make_map_3d(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Du8, d, Ld, B, 128, kI8Tokens,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return FM_ERR_LAUNCH;
-  return a.N == 64 ? launch_int8_gq<1>(tu, a, smem, stream) : launch_int8_gq<2>(tu, a, smem, stream);
+  // 8 epilogue warps for a 32-row query; 4 for 64 rows (register budget)
+  return a.N == 64 ? launch_int8_gq<1, 8>(tu, a, smem, stream) : launch_int8_gq<2, 4>(tu, a, smem, stream);
 }
 
 }  // namespace

@@ -36,8 +36,11 @@
 
 namespace fm {
 
-constexpr int kThreadsI8Fast = 6 * 32;
-constexpr int kI8Tokens = 128;  // tokens per chunk = MMA M
+// two warps + 4 or 8 epilogue warps (8: two per TMEM lane quarter taking
+// alternate chunks, so every scheduler has two independent epilogue warps)
+__host__ __device__ constexpr int i8_threads(int epi_warps) { return (2 + epi_warps) * 32; }
+constexpr int kI8Tokens = 256;  // tokens per chunk (one TMA box)
+constexpr int kI8Half = 128;    // tokens per MMA (M); a chunk is two M blocks
 constexpr int kI8Xch = 8;       // per-document exchange slots of the epilogue
 
 struct Int8Args {
@@ -52,10 +55,11 @@ struct Int8Args {
   int N;                   // MMA N = 2 parts x 32 x GQ
   int atoms;               // 128-element K atoms (ceil(d / 128))
   int nu;                  // uint8 ring slots
-  int nts;                 // TMEM slots (N columns each)
+  int nts;                 // TMEM slots (two halves of N columns each)
   size_t sc_total_bytes;   // bytes of the scales tensor (B * Ld * 2)
   uint32_t sc_slot_bytes;  // fp16 scale span + min span of one chunk
   uint32_t off_q, off_u, off_sc, off_misc, off_bar, u_slot_bytes;
+  int dbg;                 // tuning experiments only: bit 0 skip epilogue math, bit 1 skip MMAs
 };
 
 __device__ __forceinline__ int i8_len(const Int8Args& a, int b) {
@@ -89,8 +93,8 @@ __device__ __forceinline__ void spin_drain(uint32_t bar, uint32_t parity, const 
   }
 }
 
-template <int GQ>
-__global__ void __launch_bounds__(kThreadsI8Fast, 1)
+template <int GQ, int EW>
+__global__ void __launch_bounds__(i8_threads(EW), 1)
     maxsim_int8_kernel(const __grid_constant__ CUtensorMap tmap_u, const Int8Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -114,20 +118,20 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
 
   float* a256_s = reinterpret_cast<float*>(smem + a.off_misc);  // [64] alpha / 256 per query row
   float* qsum_s = a256_s + 64;                                   // [64]
-  float* xch = qsum_s + 64;                                      // [kI8Xch docs][4 warps][GQ][32]
-  int* cnt = reinterpret_cast<int*>(xch + kI8Xch * 4 * GQ * 32); // [kI8Xch] arrivals
+  float* xch = qsum_s + 64;                                      // [kI8Xch docs][EW warps][GQ][32]
+  int* cnt = reinterpret_cast<int*>(xch + kI8Xch * EW * GQ * 32); // [kI8Xch] arrivals
   volatile int* done = cnt + kI8Xch;                             // [kI8Xch] combined generations
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.nu; ++i) {
       mbar_init(u_full(i), 1);       // producer's expect_tx arrival + transaction bytes
-      mbar_init(u_empty(i), 1 + 4);  // MMA commit + the four epilogue warps
+      mbar_init(u_empty(i), 1 + 4);  // MMA commit + the four epilogue warps of the chunk
     }
     for (int i = 0; i < a.nts; ++i) {
       mbar_init(t_full(i), 1);
       mbar_init(t_empty(i), 4);
     }
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, EW);
     mbar_init(drain, 1);
     *abort_flag = 0;
     for (int i = 0; i < kI8Xch; ++i) {
@@ -170,9 +174,9 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
           const size_t lo16 = byte0 & ~static_cast<size_t>(15);
           const uint32_t span =
               static_cast<uint32_t>((byte0 + kI8Tokens * 2 - lo16 + 15) & ~static_cast<size_t>(15));
-          const bool bulk_ok = lo16 + span <= a.sc_total_bytes;
+          const bool bulk_ok = lo16 + span <= a.sc_total_bytes && !(a.dbg & 4);
           uint8_t* stage = smem + a.off_sc + ur.idx * a.sc_slot_bytes;
-          if (!bulk_ok) {
+          if (!bulk_ok && !(a.dbg & 4)) {
             // the span would run past the end of the tensors: plain loads (last chunk)
             __half* ss = reinterpret_cast<__half*>(stage);
             __half* ms = reinterpret_cast<__half*>(stage + a.sc_slot_bytes / 2);
@@ -227,12 +231,15 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
           tc_fence_after();
           FM_PROF_T0(pm0);
           const uint64_t au = smem_desc_sw128(sbase + a.off_u + ur.idx * a.u_slot_bytes);
-          const uint32_t tacc = tmem_base + tr.idx * a.N;
-          for (int at = 0; at < a.atoms; ++at) {
+          const uint32_t tacc = tmem_base + tr.idx * 2 * a.N;
+          for (int hb = 0; hb < 2; ++hb) {  // rows [128 hb, 128 hb + 128) of the chunk
+            const uint64_t ah = au + hb * (kI8Half * 128u >> 4);
+            for (int at = 0; at < a.atoms && !(a.dbg & 2); ++at) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per step, 4 steps per 128-byte atom
-              tc_mma_i8(tacc, au + at * u_atom + kk * 2u, bq + at * q_atom + kk * 2u, idesc,
-                        (at | kk) ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per step, 4 steps per 128-byte atom
+                tc_mma_i8(tacc + hb * a.N, ah + at * u_atom + kk * 2u, bq + at * q_atom + kk * 2u,
+                          idesc, (at | kk) ? 1u : 0u);
+            }
           }
           tc_commit(t_full(tr.idx));
           tc_commit(u_empty(ur.idx));
@@ -247,27 +254,34 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
   } else {
     // ===================== epilogue =====================
     const int sub = warp & 3;  // TMEM lane quarter = tokens [32 sub, 32 sub + 32) of a chunk
-    const int et = threadIdx.x - 64;
-    // --- split the query into two signed 8-bit parts: B row r = part * 32 GQ + query row ---
+    const int et = threadIdx.x - 64;  // 0 .. 32 EW - 1
+    // --- split the query into two signed 8-bit parts: B row r = part * 32 GQ + query row;
+    //     one alpha = max|Q| / 127 for the whole query ---
     {
       const int r = et;
-      if (r < a.N) {
-        const int qrow = r % (32 * GQ);
-        const int part = r / (32 * GQ);
-        const bool rv = qrow < a.Lq;
-        const __half* qr = a.q + static_cast<size_t>(rv ? qrow : 0) * a.d;
-        float amax = 0.f, qs = 0.f;
-        if (rv)
-          for (int k = 0; k < a.d; ++k) {
-            const float v = __half2float(qr[k]);
-            amax = fmaxf(amax, fabsf(v));
-            qs += v;
-          }
-        const float alpha = amax > 0.f ? amax / 127.f : 1.f;
-        if (part == 0) {
-          a256_s[qrow] = rv ? alpha * (1.f / 256.f) : 0.f;
-          qsum_s[qrow] = qs;
+      const bool builder = r < a.N;
+      const int qrow = builder ? r % (32 * GQ) : 0;
+      const int part = builder ? r / (32 * GQ) : 0;
+      const bool rv = builder && qrow < a.Lq;
+      const __half* qr = a.q + static_cast<size_t>(rv ? qrow : 0) * a.d;
+      float amax = 0.f, qs = 0.f;
+      if (rv)
+        for (int k = 0; k < a.d; ++k) {
+          const float v = __half2float(qr[k]);
+          amax = fmaxf(amax, fabsf(v));
+          qs += v;
         }
+      if (builder && part == 0) {
+        a256_s[qrow] = amax;  // row max for now
+        qsum_s[qrow] = qs;
+      }
+      named_bar_sync(1, 32 * EW);
+      float gmax = 0.f;
+      for (int j = 0; j < 32 * GQ; ++j) gmax = fmaxf(gmax, a256_s[j]);
+      const float alpha = gmax > 0.f ? gmax / 127.f : 1.f;
+      named_bar_sync(1, 32 * EW);
+      if (builder && part == 0) a256_s[qrow] = alpha * (1.f / 256.f);
+      if (builder) {
         uint8_t* row = smem + a.off_q + r * 128;
         for (int at = 0; at < a.atoms; ++at) {
           for (int c16 = 0; c16 < 8; ++c16) {
@@ -295,20 +309,20 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
         }
       }
       fence_proxy_async_smem();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * EW);
       if (lane == 0) mbar_arrive(q_ready);
     }
-    // per query row constants (the same for every lane)
-    float a256[32 * GQ], qsm[32 * GQ];
+    // query constants (the same for every lane): alpha / 256 and per-row sum_k Q
+    const float a256 = a256_s[0];
+    float qsm[32 * GQ];
 #pragma unroll
-    for (int j = 0; j < 32 * GQ; ++j) {
-      a256[j] = a256_s[j];
-      qsm[j] = qsum_s[j];
-    }
+    for (int j = 0; j < 32 * GQ; ++j) qsm[j] = qsum_s[j];
+    const int half = (EW == 8) ? (warp - 2) / 4 : 0;  // which alternate chunks this warp takes
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     const int tok_in_chunk = sub * 32 + lane;
     Ring ur, tr;
     int dloc = 0;
+    int kglob = 0;  // chunk counter of this CTA
     bool ok = true;
     for (int b = w0; b < a.B && ok; b += wstep, ++dloc) {
       const int len = i8_len(a, b);
@@ -317,34 +331,44 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
       float rmax[32 * GQ];
 #pragma unroll
       for (int j = 0; j < 32 * GQ; ++j) rmax[j] = -INFINITY;
-      for (int c = 0; c < nch; ++c) {
+      for (int c = 0; c < nch; ++c, ++kglob) {
+        if (EW == 8 && (kglob & 1) != half) {  // the other warp of this lane quarter takes it
+          tr.next(a.nts);
+          ur.next(a.nu);
+          continue;
+        }
         // u_full also publishes the chunk's scales/mins; the slot is not refilled
         // before this warp releases it below
         if (!mbar_wait(u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
         if (!mbar_wait(t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) { ok = false; break; }
         tc_fence_after();
         FM_PROF_T0(pe0);
-        const uint32_t th = tmem_base + lane_base + tr.idx * a.N;
-        const int tok = c * kI8Tokens + tok_in_chunk;
-        const bool valid = tok < len;
-        const bool full = (c + 1) * kI8Tokens <= len;  // whole chunk valid (warp-uniform)
         const size_t byte0 = (static_cast<size_t>(b) * a.Ld + static_cast<size_t>(c) * kI8Tokens) * 2;
-        const int sh = static_cast<int>((byte0 & 15) >> 1) + tok_in_chunk;
         const uint8_t* stage = smem + a.off_sc + ur.idx * a.sc_slot_bytes;
-        const float s_t = __half2float(reinterpret_cast<const __half*>(stage)[sh]);
-        const float m_t = __half2float(reinterpret_cast<const __half*>(stage + a.sc_slot_bytes / 2)[sh]);
+        const bool full = (c + 1) * kI8Tokens <= len;  // whole chunk valid (warp-uniform)
 #pragma unroll
-        for (int g = 0; g < GQ; ++g) {
-          uint32_t h[32], l[32];
-          tmem_ld32(th + g * 32, reinterpret_cast<float(&)[32]>(h));
-          tmem_ld32(th + 32 * GQ + g * 32, reinterpret_cast<float(&)[32]>(l));
-          tmem_wait_ld();
-          if (full || valid) {
+        for (int hb = 0; hb < 2; ++hb) {
+          const int tic = hb * kI8Half + tok_in_chunk;
+          const bool valid = c * kI8Tokens + tic < len;
+          if (!full && !__any_sync(0xffffffffu, valid)) continue;
+          const uint32_t th = tmem_base + lane_base + tr.idx * 2 * a.N + hb * a.N;
+          const int sh = static_cast<int>((byte0 & 15) >> 1) + tic;
+          const float s_t = __half2float(reinterpret_cast<const __half*>(stage)[sh]);
+          const float m_t = __half2float(reinterpret_cast<const __half*>(stage + a.sc_slot_bytes / 2)[sh]);
+          const float sa = s_t * a256;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int hl = static_cast<int>(h[j]) * 256 + static_cast<int>(l[j]);  // exact
-              const float sv = fmaf(s_t * a256[g * 32 + j], static_cast<float>(hl), m_t * qsm[g * 32 + j]);
-              rmax[g * 32 + j] = fmaxf(rmax[g * 32 + j], sv);
+          for (int g = 0; g < GQ; ++g) {
+            uint32_t h[32], l[32];
+            tmem_ld32(th + g * 32, reinterpret_cast<float(&)[32]>(h));
+            tmem_ld32(th + 32 * GQ + g * 32, reinterpret_cast<float(&)[32]>(l));
+            tmem_wait_ld();
+            if ((full || valid) && !(a.dbg & 1)) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int hl = static_cast<int>(h[j]) * 256 + static_cast<int>(l[j]);  // exact
+                const float sv = fmaf(sa, static_cast<float>(hl), m_t * qsm[g * 32 + j]);
+                rmax[g * 32 + j] = fmaxf(rmax[g * 32 + j], sv);
+              }
             }
           }
         }
@@ -387,7 +411,8 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
         __threadfence_block();
       }
 #pragma unroll
-      for (int g = 0; g < GQ; ++g) xch[((slot * 4 + sub) * GQ + g) * 32 + lane] = acc[g];
+      const int ew = warp - 2;
+      for (int g = 0; g < GQ; ++g) xch[((slot * EW + ew) * GQ + g) * 32 + lane] = acc[g];
       __syncwarp();
       int old = 0;
       if (lane == 0) {
@@ -395,13 +420,13 @@ __global__ void __launch_bounds__(kThreadsI8Fast, 1)
         old = atomicAdd(&cnt[slot], 1);
       }
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == 3) {
+      if (old == EW - 1) {
         __threadfence_block();
         float tot = 0.f;
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
           float mm = -INFINITY;
-          for (int w = 0; w < 4; ++w) mm = fmaxf(mm, xch[((slot * 4 + w) * GQ + g) * 32 + lane]);
+          for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
           tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
         }
         tot = warp_sum(tot);
