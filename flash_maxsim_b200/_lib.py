@@ -34,7 +34,8 @@ SIGNATURES = {
     "fm_maxsim_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_int8_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_sparse_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
-    "fm_maxsim_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "fm_maxsim_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64, _P]),
+    "fm_maxsim_bwd_workspace_size": (_I64, [_I, _I, _I, _I, _I]),
     "fm_quantize_int8": (_I, [_P, _I, _P, _P, _P, _I64, _I, _P]),
     "fm_wait_selftest": (_I, [_P, _I64, _P]),
     "fm_fwd_plan_info": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I]),

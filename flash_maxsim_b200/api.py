@@ -179,10 +179,13 @@ class _FlashMaxSimFn(torch.autograd.Function):
         grad_Q = torch.empty(Nq, Lq, dp, device=Qh.device, dtype=torch.float16)
         grad_D = torch.empty(B, Ld, dp, device=Dh.device, dtype=torch.float16)
         dev = Qh.device
+        ws_bytes = int(lib.fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, dp))
+        ws = torch.empty(max(ws_bytes, 0) // 4, device=dev, dtype=torch.float32) if ws_bytes > 0 else None
         with torch.cuda.device(dev):
             rc = lib.fm_maxsim_bwd(
                 Qh.data_ptr(), Dh.data_ptr(), argmax.data_ptr(), g.data_ptr(),
-                grad_Q.data_ptr(), grad_D.data_ptr(), Nq, B, Lq, Ld, dp, _lib.stream_of(dev))
+                grad_Q.data_ptr(), grad_D.data_ptr(), Nq, B, Lq, Ld, dp,
+                _lib.ptr(ws), ws_bytes, _lib.stream_of(dev))
         _lib.check(rc, "fm_maxsim_bwd")
         _after_call(dev)
         grad_Q = grad_Q[..., :d]

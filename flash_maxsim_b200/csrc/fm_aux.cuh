@@ -43,55 +43,101 @@ __device__ __forceinline__ uint4 pack8(const float (&acc)[8]) {
   return r;
 }
 
-// dQ: grid (Nq, ceil(Lq / 8)), 8 warps; warp = one query row, lanes span d
-// (8 fp16 per lane per 256-element segment).  Loops over documents in order.
+// dQ partial sums: grid (ceil(Nq * Lq / 8) row tiles, nsplit document ranges);
+// warp = one query row (n, q), lanes span d (8 fp16 per lane per 256-element
+// segment).  Documents of the range are visited in order, four gathers in
+// flight.  With nsplit == 1 the row is written as fp16 directly; otherwise
+// the fp32 partial goes to ws[split][row][d] and maxsim_bwd_dq_reduce adds
+// the splits in order.  blockIdx.x (row tiles) varies fastest, so the CTAs
+// that run together read the same document range (L2-resident).
+template <int NSEG>
 __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dq_kernel(
     const __half* __restrict__ D, const int32_t* __restrict__ am, const float* __restrict__ g,
-    __half* __restrict__ dQ, int Nq, int B, int Lq, int Ld, int d, int shared) {
-  const int n = blockIdx.x;
-  const int q = blockIdx.y * 8 + (threadIdx.x >> 5);
+    __half* __restrict__ dQ, float* __restrict__ ws, int Nq, int B, int Lq, int Ld, int d,
+    int docs_per_split) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (q >= Lq) return;
-  const int nseg = (d + 255) / 256;
-  float acc[kMaxSeg][8];
+  const int rows = Nq * Lq;
+  if (row >= rows) return;
+  const int n = row / Lq, q = row - n * Lq;
+  const int b_lo = blockIdx.y * docs_per_split;
+  const int b_hi = min(B, b_lo + docs_per_split);
+  constexpr int nseg = NSEG;
+  float acc[NSEG][8];
 #pragma unroll
-  for (int s = 0; s < kMaxSeg; ++s)
+  for (int s = 0; s < NSEG; ++s)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[s][j] = 0.f;
 
-  for (int b0 = 0; b0 < B; b0 += 32) {
+  for (int b0 = b_lo; b0 < b_hi; b0 += 32) {
     const int bl = b0 + lane;
     int t = -1;
     float gv = 0.f;
-    if (bl < B) {
+    if (bl < b_hi) {
       const size_t pair = static_cast<size_t>(n) * B + bl;
       t = __ldg(am + pair * Lq + q);
       gv = __ldg(g + pair);
     }
-    const int nb = min(32, B - b0);
-    for (int i = 0; i < nb; ++i) {
-      const int ti = __shfl_sync(0xffffffffu, t, i);
-      const float gi = __shfl_sync(0xffffffffu, gv, i);
-      if (ti < 0) continue;
-      const size_t doc = shared ? static_cast<size_t>(b0 + i) : static_cast<size_t>(n) * B + b0 + i;
-      const __half* row = D + (doc * Ld + ti) * static_cast<size_t>(d);
+    const int nb = min(32, b_hi - b0);
+    for (int i = 0; i < nb; i += 4) {
+      uint4 raw[4][NSEG];
+      float gi[4];
 #pragma unroll
-      for (int s = 0; s < kMaxSeg; ++s) {
-        if (s < nseg) {
+      for (int u = 0; u < 4; ++u) {
+        const int ti = __shfl_sync(0xffffffffu, t, (i + u) & 31);
+        gi[u] = __shfl_sync(0xffffffffu, gv, (i + u) & 31);
+        const bool use = (i + u < nb) && ti >= 0;
+        if (!use) gi[u] = 0.f;
+        const __half* rowp = D + (static_cast<size_t>(b0 + i + u) * Ld + (use ? ti : 0)) * static_cast<size_t>(d);
+#pragma unroll
+        for (int s = 0; s < NSEG; ++s) {
           const int k = s * 256 + lane * 8;
-          if (k < d) fma8(acc[s], __ldg(reinterpret_cast<const uint4*>(row + k)), gi);
+          raw[u][s] = (use && s < nseg && k < d) ? __ldg(reinterpret_cast<const uint4*>(rowp + k))
+                                                 : make_uint4(0, 0, 0, 0);
         }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int s = 0; s < NSEG; ++s)
+          if (s < nseg) fma8(acc[s], raw[u][s], gi[u]);
+    }
+  }
+  if (gridDim.y == 1) {
+    __half* out = dQ + static_cast<size_t>(row) * d;
+#pragma unroll
+    for (int s = 0; s < NSEG; ++s) {
+      const int k = s * 256 + lane * 8;
+      if (s < nseg && k < d) *reinterpret_cast<uint4*>(out + k) = pack8(acc[s]);
+    }
+  } else {
+    float* out = ws + (static_cast<size_t>(blockIdx.y) * rows + row) * d;
+#pragma unroll
+    for (int s = 0; s < NSEG; ++s) {
+      const int k = s * 256 + lane * 8;
+      if (s < nseg && k < d) {
+        *reinterpret_cast<float4*>(out + k) = make_float4(acc[s][0], acc[s][1], acc[s][2], acc[s][3]);
+        *reinterpret_cast<float4*>(out + k + 4) = make_float4(acc[s][4], acc[s][5], acc[s][6], acc[s][7]);
       }
     }
   }
-  __half* out = dQ + (static_cast<size_t>(n) * Lq + q) * d;
+}
+
+// dQ[row][k] = sum over splits (in order) of ws[split][row][k], rounded to fp16.
+__global__ void __launch_bounds__(256) maxsim_bwd_dq_reduce(const float* __restrict__ ws,
+                                                            __half* __restrict__ dQ, int64_t n8, int nsplit) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;  // group of 8 elements
+  if (i >= n8) return;
+  float acc[8];
 #pragma unroll
-  for (int s = 0; s < kMaxSeg; ++s) {
-    if (s < nseg) {
-      const int k = s * 256 + lane * 8;
-      if (k < d) *reinterpret_cast<uint4*>(out + k) = pack8(acc[s]);
-    }
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float4* p = reinterpret_cast<const float4*>(ws + (static_cast<int64_t>(s) * n8 + i) * 8);
+    const float4 x = __ldg(p), y = __ldg(p + 1);
+    acc[0] += x.x; acc[1] += x.y; acc[2] += x.z; acc[3] += x.w;
+    acc[4] += y.x; acc[5] += y.y; acc[6] += y.z; acc[7] += y.w;
   }
+  *reinterpret_cast<uint4*>(dQ + i * 8) = pack8(acc);
 }
 
 // dD: one CTA per document.  The (query, row) entries that picked a token of

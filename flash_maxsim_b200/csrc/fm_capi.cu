@@ -477,9 +477,33 @@ int fm_maxsim_sparse_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* in
                     static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+namespace fm {
+namespace {
+// Document ranges of the dQ pass: enough CTAs to fill the GPU (>= 2 per SM),
+// ranges whose documents fit comfortably in L2 (<= 64 MB), >= 8 docs each.
+int dq_splits(int Nq, int B, int Lq, int Ld, int d) {
+  const int tiles = cdiv(Nq * Lq, 8);
+  const int64_t doc_bytes = static_cast<int64_t>(Ld) * d * 2;
+  int ns = std::max(cdiv(296, tiles), static_cast<int>((doc_bytes * B + (64ll << 20) - 1) / (64ll << 20)));
+  ns = std::min(ns, std::max(1, B / 8));
+  return std::max(1, ns);
+}
+}  // namespace
+}  // namespace fm
+
+extern "C" {
+
+int64_t fm_maxsim_bwd_workspace_size(int Nq, int B, int Lq, int Ld, int d) {
+  if (Nq < 1 || B < 1 || Lq < 1 || Ld < 1 || d < 8) return 0;
+  const int ns = dq_splits(Nq, B, Lq, Ld, d);
+  return ns > 1 ? static_cast<int64_t>(ns) * Nq * Lq * d * 4 : 0;
+}
+
 int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
                   const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
-                  int Lq, int Ld, int d, void* stream) {
+                  int Lq, int Ld, int d, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!Q || !D || !argmax || !grad_scores || !grad_Q || !grad_D) return FM_ERR_ARG;
   if (Nq < 1 || B < 0 || Lq < 1 || Ld < 1 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
   if (!aligned16(Q) || !aligned16(D) || !aligned16(grad_Q) || !aligned16(grad_D)) return FM_ERR_ARG;
@@ -492,11 +516,31 @@ int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
     // no documents: dQ is zero
     return cudaMemsetAsync(grad_Q, 0, E * d * 2, st) == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
   }
-  dim3 gq(Nq, cdiv(Lq, 8));
-  maxsim_bwd_dq_kernel<<<gq, kBwdThreads, 0, st>>>(
-      reinterpret_cast<const __half*>(D), argmax, grad_scores, reinterpret_cast<__half*>(grad_Q),
-      Nq, B, Lq, Ld, d, 1);
-  if (cudaGetLastError() != cudaSuccess) return FM_ERR_LAUNCH;
+  const int64_t need = fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, d);
+  if (need > 0 && (!workspace || workspace_bytes < need || !aligned16(workspace))) return FM_ERR_ARG;
+  const int ns = need > 0 ? dq_splits(Nq, B, Lq, Ld, d) : 1;
+  const int per = cdiv(B, ns);
+  dim3 gq(cdiv(static_cast<int>(E), 8), ns);
+  const __half* Dh = reinterpret_cast<const __half*>(D);
+  __half* dQh = reinterpret_cast<__half*>(grad_Q);
+  float* ws = static_cast<float*>(workspace);
+  if (!(tune().dbg & 32)) {
+    const int nseg = cdiv(d, 256);
+    if (nseg == 1)
+      maxsim_bwd_dq_kernel<1><<<gq, kBwdThreads, 0, st>>>(Dh, argmax, grad_scores, dQh, ws, Nq, B, Lq, Ld, d, per);
+    else if (nseg == 2)
+      maxsim_bwd_dq_kernel<2><<<gq, kBwdThreads, 0, st>>>(Dh, argmax, grad_scores, dQh, ws, Nq, B, Lq, Ld, d, per);
+    else if (nseg <= 4)
+      maxsim_bwd_dq_kernel<4><<<gq, kBwdThreads, 0, st>>>(Dh, argmax, grad_scores, dQh, ws, Nq, B, Lq, Ld, d, per);
+    else
+      maxsim_bwd_dq_kernel<8><<<gq, kBwdThreads, 0, st>>>(Dh, argmax, grad_scores, dQh, ws, Nq, B, Lq, Ld, d, per);
+    if (cudaGetLastError() != cudaSuccess) return FM_ERR_LAUNCH;
+    if (ns > 1) {
+      const int64_t n8 = E * d / 8;
+      maxsim_bwd_dq_reduce<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, st>>>(ws, dQh, n8, ns);
+      if (cudaGetLastError() != cudaSuccess) return FM_ERR_LAUNCH;
+    }
+  }
   static std::atomic<bool> dd_cfg{false};
   if (!dd_cfg.load()) {
     if (cudaFuncSetAttribute(maxsim_bwd_dd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -504,9 +548,10 @@ int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
       return FM_ERR_LAUNCH;
     dd_cfg.store(true);
   }
-  maxsim_bwd_dd_kernel<<<B, kBwdThreads, smem, st>>>(
-      reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D),
-      Nq, B, Lq, Ld, d);
+  if (!(tune().dbg & 16))
+    maxsim_bwd_dd_kernel<<<B, kBwdThreads, smem, st>>>(
+        reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D), Nq,
+        B, Lq, Ld, d);
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 

@@ -114,15 +114,19 @@ int fm_maxsim_sparse_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* in
  *   grad_Q[n,q,:] = sum_b g[n,b] * D[b, argmax[n,b,q], :]
  *   grad_D[b,t,:] = sum_{(n,q): argmax[n,b,q]==t} g[n,b] * Q[n,q,:]
  * grad_scores: fp32 [Nq, B]. grad_Q: fp16 [Nq, Lq, d], grad_D: fp16
- * [B, Ld, d]; both fully written (no pre-zeroing needed). Deterministic.
- * Requires Nq * Lq <= 32768.
+ * [B, Ld, d]; both fully written (no pre-zeroing needed). Deterministic:
+ * grad_Q is summed over document ranges in fp32 partials (workspace) that are
+ * added in a fixed order. workspace: caller-owned device memory of at least
+ * fm_maxsim_bwd_workspace_size(...) bytes, 16-byte aligned (NULL allowed when
+ * that size is 0). Requires Nq * Lq <= 32768.
  * Replaces `_maxsim_bwd_dQ_kernel` and `_maxsim_bwd_dD_kernel` launched by
  *   _FlashMaxSimFn.backward (flash_maxsim/flash_maxsim.py:266-286,
  *   kernels :153-188).
  */
+int64_t fm_maxsim_bwd_workspace_size(int Nq, int B, int Lq, int Ld, int d);
 int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
                   const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
-                  int Lq, int Ld, int d, void* stream);
+                  int Lq, int Ld, int d, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* element types accepted by fm_quantize_int8 */
 #define FM_DTYPE_F16 0

@@ -41,7 +41,8 @@ def test_argument_errors_without_device():
     assert L.fm_maxsim_fwd(None, None, None, None, None, 1, 1, 32, 300, 128, 1, None, None) == _lib.FM_ERR_ARG
     assert L.fm_maxsim_int8_fwd(None, None, None, None, None, None, 1, 32, 300, 128, None, None) == _lib.FM_ERR_ARG
     assert L.fm_maxsim_sparse_fwd(None, None, None, None, None, 1, 4, 32, 300, 128, None, None) == _lib.FM_ERR_ARG
-    assert L.fm_maxsim_bwd(None, None, None, None, None, None, 1, 1, 32, 300, 128, None) == _lib.FM_ERR_ARG
+    assert L.fm_maxsim_bwd(None, None, None, None, None, None, 1, 1, 32, 300, 128, None, 0, None) == _lib.FM_ERR_ARG
+    assert L.fm_maxsim_bwd_workspace_size(64, 4096, 64, 1024, 256) > 0
     assert L.fm_quantize_int8(None, 0, None, None, None, 10, 128, None) == _lib.FM_ERR_ARG
     assert L.fm_wait_selftest(None, 1000, None) == _lib.FM_ERR_ARG
 
