@@ -19,6 +19,7 @@ FM_ERR_LAUNCH = 2
 FM_ERR_TIMEOUT_SELFTEST = 19
 FM_ERR_BAD_INDEX = 20
 FM_ERR_UNSUPPORTED = 21
+FM_ERR_SCRATCH_TOO_SMALL = 23
 FM_DTYPE_F16 = 0
 FM_DTYPE_F32 = 1
 FM_DTYPE_BF16 = 2
@@ -36,6 +37,7 @@ SIGNATURES = {
     "fm_maxsim_sparse_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64, _P]),
     "fm_maxsim_bwd_workspace_size": (_I64, [_I, _I, _I, _I, _I]),
+    "fm_maxsim_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "fm_quantize_int8": (_I, [_P, _I, _P, _P, _P, _I64, _I, _P]),
     "fm_wait_selftest": (_I, [_P, _I64, _P]),
     "fm_fwd_plan_info": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I]),

@@ -17,6 +17,14 @@
 #include "fm_fwd.cuh"
 #include "fm_int8.cuh"
 
+// Scratch for fm_maxsim_bwd_noalloc: the dQ partial sums live here instead of
+// in caller-provided memory.  Every device that loads this library keeps
+// these 16 MiB for the life of the process.  In host code the name below is
+// only a host-side handle; the device address comes from
+// cudaGetSymbolAddress (see noalloc_scratch()).
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(16) << 20;
+static __device__ __align__(256) float g_fm_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
 namespace fm {
 namespace {
 
@@ -425,6 +433,8 @@ const char* fm_status_string(int code) {
     case FM_ERR_BAD_INDEX: return "sparse query index out of range";
     case FM_ERR_UNSUPPORTED: return "shape not supported by the sm_100a kernels";
     case FM_ERR_NO_DEVICE: return "no CUDA device";
+    case FM_ERR_SCRATCH_TOO_SMALL:
+      return "shape needs more dQ workspace than the 16 MiB built-in scratch of fm_maxsim_bwd_noalloc";
   }
   return "unknown status";
 }
@@ -553,6 +563,32 @@ int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
         reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D), Nq,
         B, Lq, Ld, d);
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int fm_maxsim_bwd_noalloc(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
+                          const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq,
+                          int B, int Lq, int Ld, int d, void* stream) {
+  // the size limit is checked first, before any pointer is looked at
+  const int64_t need = fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, d);
+  if (need > static_cast<int64_t>(kNoAllocScratchBytes)) return FM_ERR_SCRATCH_TOO_SMALL;
+  void* scratch = nullptr;
+  if (need > 0) {
+    // Device address of the built-in scratch for the current device, looked up
+    // once per device (with that device current) and cached.
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FM_ERR_NO_DEVICE;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_fm_noalloc_scratch) != cudaSuccess || !p) return FM_ERR_LAUNCH;
+      addr[dev] = p;
+    }
+    scratch = addr[dev];
+  }
+  return fm_maxsim_bwd(Q, D, argmax, grad_scores, grad_Q, grad_D, Nq, B, Lq, Ld, d, scratch,
+                       static_cast<int64_t>(kNoAllocScratchBytes), stream);
 }
 
 int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,

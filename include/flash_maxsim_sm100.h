@@ -44,6 +44,7 @@ extern "C" {
 #define FM_ERR_BAD_INDEX 20
 #define FM_ERR_UNSUPPORTED 21
 #define FM_ERR_NO_DEVICE 22
+#define FM_ERR_SCRATCH_TOO_SMALL 23
 
 /* ABI version of this header (major * 100 + minor). */
 int fm_abi_version(void);
@@ -127,6 +128,26 @@ int64_t fm_maxsim_bwd_workspace_size(int Nq, int B, int Lq, int Ld, int d);
 int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
                   const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
                   int Lq, int Ld, int d, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Same backward as fm_maxsim_bwd for callers that cannot allocate device
+ * memory -- for example a host program that hands this library only the
+ * tensors it already owns, inside an engine whose device memory is fully
+ * reserved by its own allocator, or that must not allocate once serving has
+ * started. Nothing is allocated: the dQ partial sums go to a 16 MiB scratch
+ * array compiled into the library (every device that loads the library keeps
+ * it until the process exits). Shapes whose workspace
+ * (fm_maxsim_bwd_workspace_size) exceeds 16 MiB are rejected with
+ * FM_ERR_SCRATCH_TOO_SMALL. The first call on a device looks up the scratch
+ * address for that device; make that first call before any stream capture.
+ * All calls share the one scratch array, so calls that overlap on the GPU
+ * (different streams, or different host threads) race; serialise them. Every
+ * partial sum is written before it is read, so nothing needs clearing between
+ * calls. No counterpart in the reference.
+ */
+int fm_maxsim_bwd_noalloc(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
+                          const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq,
+                          int B, int Lq, int Ld, int d, void* stream);
 
 /* element types accepted by fm_quantize_int8 */
 #define FM_DTYPE_F16 0
