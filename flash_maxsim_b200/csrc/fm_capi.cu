@@ -163,7 +163,7 @@ bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
   const int mb_total = cdiv(a.R, 4);
 
   const int rows_bytes = round_up(a.rowbuf * 4, 16);
-  const int xch_bytes = 128 * 8;
+  const int xch_bytes = 128 * 8 + 2 * 128 * 8;  // column-part exchange + double-buffered pair exchange
   const int qsum_bytes = int8 ? round_up(a.Gq * 32 * 4, 16) : 0;
   const int state_per_mb = 128 * 4 * (s.argmax ? 2 : 1);
 

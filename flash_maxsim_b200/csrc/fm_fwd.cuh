@@ -49,10 +49,11 @@ namespace fm {
 
 enum FwdMode : int { MODE_DENSE = 0, MODE_SPARSE = 1, MODE_INT8 = 2 };
 
-constexpr int kEpiWarp0 = 2;
+constexpr int kEpiWarp0 = 2;   // epilogue warps 2..5
 constexpr int kQProdWarp = 6;
-constexpr int kConvWarp0 = 7;
-constexpr int kThreadsF16 = 7 * 32;
+constexpr int kEpiWarp1 = 7;   // second epilogue set 7..10 (fp16 modes): odd query blocks
+constexpr int kConvWarp0 = 7;  // INT8 converters 7..10
+constexpr int kThreadsF16 = 11 * 32;
 constexpr int kThreadsI8 = 11 * 32;
 constexpr int kMaxGroupDocs = 8;
 
@@ -272,37 +273,32 @@ __device__ __forceinline__ void epi_piece(float (&v)[32], int nv, int col0, cons
 }
 
 // Row max over the first `valid` columns of one accumulator slot, plain fp16
-// scoring (no argmax, no INT8 map): full 32-column pieces two per TMEM wait,
-// then the ragged tail masked with -inf.  Compact on purpose: the epilogue
-// runs one warp per scheduler, so its instruction count sets its speed.
-__device__ __forceinline__ void chunk_max_plain(uint32_t taddr, int valid, RowAcc<false>& acc) {
+// scoring (no argmax, no INT8 map), 32-column pieces first, first + step, ...
+// (step 2 when two warps share a lane quarter): full pieces two per TMEM wait,
+// ragged tail masked with -inf.  Compact on purpose: the epilogue is
+// latency-bound, so its instruction count sets its speed.
+__device__ __forceinline__ void chunk_max_plain(uint32_t taddr, int valid, RowAcc<false>& acc, int first,
+                                                int step) {
   const int nfull = valid >> 5;
-  int q = 0;
-  for (; q + 2 <= nfull; q += 2) {
+  int q = first;
+  for (; q + step < nfull; q += 2 * step) {
     float v0[32], v1[32];
     tmem_ld32(taddr + q * 32, v0);
-    tmem_ld32(taddr + q * 32 + 32, v1);
+    tmem_ld32(taddr + (q + step) * 32, v1);
     tmem_wait_ld();
     piece_max<false>(v0, 32, 0, acc);
     piece_max<false>(v1, 32, 0, acc);
   }
-  const int rem = valid - q * 32;  // 0..63 columns left
-  if (rem > 0) {
+  for (; q * 32 < valid; q += step) {
     float v0[32];
     tmem_ld32(taddr + q * 32, v0);
     tmem_wait_ld();
+    const int rem = valid - q * 32;
     if (rem < 32) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v0[i] = i < rem ? v0[i] : -INFINITY;
     }
     piece_max<false>(v0, 32, 0, acc);
-    if (rem > 32) {
-      tmem_ld32(taddr + q * 32 + 32, v0);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v0[i] = i < rem - 32 ? v0[i] : -INFINITY;
-      piece_max<false>(v0, 32, 0, acc);
-    }
   }
 }
 
@@ -361,7 +357,8 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
     }
     for (int i = 0; i < a.nts; ++i) {
       mbar_init(bars.t_full(i), 1);
-      mbar_init(bars.t_empty(i), 4);
+      // every epilogue warp that reads the slot releases it
+      mbar_init(bars.t_empty(i), (MODE != MODE_INT8 && a.rep == 1) ? 8 : 4);
     }
     if (MODE == MODE_INT8) {
       for (int i = 0; i < a.nu; ++i) {
@@ -656,9 +653,25 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       tc_commit(bars.drain());
       drain_wait(bars.drain(), 0, a);
     }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+  } else if ((warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) ||
+             (MODE != MODE_INT8 && warp >= kEpiWarp1 && warp < kEpiWarp1 + 4)) {
     // ===================== epilogue =====================
-    const int et = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    // fp16 modes run two sets of four warps (one warp per TMEM lane quarter in
+    // each set), so every scheduler has two epilogue warps to switch between.
+    // Without column replication (rep == 1) both warps of a lane quarter read
+    // every chunk, taking alternate 32-column pieces, and merge their row maxima
+    // per (M-block, document) through a double-buffered exchange and a 64-thread
+    // barrier per quarter.  With replication (rep > 1) the second set idles.
+    constexpr int EW = (MODE == MODE_INT8) ? 4 : 8;
+    const int half = warp >= kEpiWarp1 ? 1 : 0;
+    const bool pair = EW == 8 && a.rep == 1;        // two warps per lane quarter split columns
+    const bool idle = EW == 8 && a.rep > 1 && half == 1;
+    const int pstep = pair ? 2 : 1;
+    const int pfirst = pair ? half : 0;
+    float* xp_m = reinterpret_cast<float*>(smem + a.off_xch + 128 * 8);  // [2 buffers][128]
+    int* xp_i = reinterpret_cast<int*>(smem + a.off_xch + 128 * 8 + 2 * 128 * 4);
+    int xbuf = 0;
+    const int et = half ? 128 + threadIdx.x - kEpiWarp1 * 32 : threadIdx.x - kEpiWarp0 * 32;  // 0..32*EW-1
     const int sub = warp & 3;                      // TMEM lane quarter
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     float* state_m = reinterpret_cast<float*>(smem + a.off_state);
@@ -682,7 +695,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         }
         qsum_s[q] = s;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * EW);
     }
     Ring tr, er;
     bool ok = true;
@@ -693,13 +706,13 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         for (int i = 0; i < it.ndocs; ++i) {
           const int b = it.b0 + i;
           if (MODE == MODE_DENSE) {
-            for (int n = et; n < it.nqi; n += 128)
+            for (int n = et; n < it.nqi; n += 32 * EW)
               a.scores[static_cast<size_t>(it.n_lo + n) * a.B + b] = -INFINITY;
           } else if (et == 0) {
             a.scores[b] = (MODE == MODE_SPARSE && a.K == 0) ? 0.f : -INFINITY;
           }
           if (ARGMAX) {
-            for (int e = et; e < it.nqi * a.Lq; e += 128) {
+            for (int e = et; e < it.nqi * a.Lq; e += 32 * EW) {
               const int n = it.n_lo + e / a.Lq;
               const int q = e - (e / a.Lq) * a.Lq;
               a.argmax[(static_cast<size_t>(n) * a.B + b) * a.Lq + q] = -1;
@@ -708,7 +721,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         }
         continue;
       }
-      for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
+      for (int s0 = it.rg_lo; s0 < it.rg_hi && ok && !idle; s0 += it.span) {
         const int s1 = min(it.rg_hi, s0 + it.span);
         const int nmb = span_mblocks(a, s0, s1);
         for (int g = 0; g < it.ngr && ok; ++g) {
@@ -752,21 +765,24 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 if (MODE != MODE_INT8 && !ARGMAX && rep == 1) {
                   if (active && !skip_epi)
                     chunk_max_plain(tmem_base + lane_base + tr.idx * a.ts_stride,
-                                    min(a.C, len - c * a.C), *reinterpret_cast<RowAcc<false>*>(&acc));
+                                    min(a.C, len - c * a.C), *reinterpret_cast<RowAcc<false>*>(&acc),
+                                    pfirst, pstep);
                 } else if (active && !skip_epi) {
                   const int tok0 = c * a.C;
                   const int valid = min(a.C, len - tok0);
                   const int npieces = (valid + 31) >> 5;
                   const uint32_t taddr = tmem_base + lane_base + tr.idx * a.ts_stride;
-                  // piece p of this chunk belongs to part ((c * ppc + p) % rep)
+                  // piece p of this chunk belongs to part ((c * ppc + p) % nparts)
+                  const int nparts = rep > 1 ? rep : pstep;
+                  const int mypart = rep > 1 ? part : pfirst;
                   int p = 0;
-                  if (rep > 1) {
-                    const int first = (c * ppc) % rep;
-                    p = (part - first + rep) % rep;
+                  if (nparts > 1) {
+                    const int first = (c * ppc) % nparts;
+                    p = (mypart - first + nparts) % nparts;
                   }
                   // two TMEM loads in flight per wait
-                  for (; p < npieces; p += 2 * rep) {
-                    const int p1 = p + rep;
+                  for (; p < npieces; p += 2 * nparts) {
+                    const int p1 = p + nparts;
                     const bool two = p1 < npieces;
                     float v0[32], v1[32];
 
@@ -788,6 +804,18 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 tr.next(a.nts);
               }
               if (!ok) break;
+              if (pair) {
+                // merge the two column halves of each row: set 1 hands over, set 0 goes on
+                if (half == 1) {
+                  xp_m[xbuf * 128 + sub * 32 + lane] = acc.m;
+                  if (ARGMAX) xp_i[xbuf * 128 + sub * 32 + lane] = acc.idx;
+                }
+                named_bar_sync(2 + sub, 64);
+                if (half == 0)
+                  acc.merge(xp_m[xbuf * 128 + sub * 32 + lane], ARGMAX ? xp_i[xbuf * 128 + sub * 32 + lane] : 0);
+                xbuf ^= 1;
+                if (half == 1) continue;
+              }
               FM_PROF_T0(pf0);
               // combine across chunk groups (single-document items)
               if (it.ngr > 1) {
@@ -841,11 +869,11 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       if (!ok) break;
       // ---- per-item finalisation (epilogue warps only) ----
       FM_PROF_T0(pi0);
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * EW);
       FM_PROF_ADD(29, pi0);
       if (rep > 1) {
         // single-document items: combine the column parts of each row
-        if (part == 0) {
+        if (part == 0 && half == 0) {
           RowAcc<ARGMAX> acc;
           acc.m = xch_m[sub * 32 + lane];
           acc.idx = ARGMAX ? xch_i[sub * 32 + lane] : 0;
@@ -865,7 +893,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
             a.argmax[(static_cast<size_t>(n) * a.B + it.b0) * a.Lq + qrow] = acc.idx;
           }
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * EW);
       }
       if (MODE == MODE_SPARSE) {
         // score = sum_k rowmax[idx[b, k]] in a fixed order
@@ -885,7 +913,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
           if (lane == 0) a.scores[it.b0] = s;
         }
       } else {
-        for (int e = et; e < it.ndocs * it.nqi; e += 128) {
+        for (int e = et; e < it.ndocs * it.nqi; e += 32 * EW) {
           const int i = e / it.nqi;
           const int n = e - i * it.nqi;
           float s = 0.f;
@@ -894,7 +922,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         }
       }
       FM_PROF_T0(pi1);
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 32 * EW);
       FM_PROF_ADD(30, pi1);
       FM_PROF_ADD(31, pi0);
     }
