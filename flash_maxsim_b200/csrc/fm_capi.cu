@@ -16,6 +16,7 @@
 #include "fm_aux.cuh"
 #include "fm_fwd.cuh"
 #include "fm_int8.cuh"
+#include "fm_q1.cuh"
 
 // Scratch for fm_maxsim_bwd_noalloc: the dQ partial sums live here instead of
 // in caller-provided memory.  Every device that loads this library keeps
@@ -274,6 +275,10 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tq2, const CUtensorMap&
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
+bool q1_ok(const Shape& s);
+int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
+              int32_t* status, cudaStream_t stream);
+
 int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
                int32_t* argmax, const int32_t* sp_idx, const void* scales, const void* mins,
                int32_t* status, cudaStream_t stream) {
@@ -287,6 +292,8 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   if (s.B == 0) return FM_OK;
   const int64_t n_docs = s.shared ? s.B : static_cast<int64_t>(s.Nq) * s.B;
   if (n_docs > INT32_MAX || static_cast<int64_t>(s.Nq) * s.B > INT32_MAX) return FM_ERR_ARG;
+
+  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, status, stream);
 
   FwdArgs a{};
   int smem = 0;
@@ -404,6 +411,81 @@ int launch_int8_fast(const void* Q, const void* Du8, const void* scales, const v
     return FM_ERR_LAUNCH;
   // 8 epilogue warps for a 32-row query; 4 for 64 rows (register budget)
   return a.N == 64 ? launch_int8_gq<1, 8>(tu, a, smem, stream) : launch_int8_gq<2, 4>(tu, a, smem, stream);
+}
+
+// Short-query path (fm_q1.cuh): one query of <= 64 rows and d <= 128 against
+// shared documents, the document chunk as the MMA's M operand.
+bool q1_ok(const Shape& s) {
+  return s.mode == MODE_DENSE && !s.argmax && s.Nq == 1 && s.Lq <= 64 && s.d <= 128 &&
+         !(tune().dbg & 8);
+}
+
+bool plan_q1(const Shape& s, int CT, Q1Args& a, int& smem) {
+  a.B = s.B;
+  a.Lq = s.Lq;
+  a.Ld = s.Ld;
+  a.d = s.d;
+  a.N = 32 * cdiv(s.Lq, 32);
+  a.atoms = cdiv(s.d, 64);
+  a.nts = 512 / ((CT / 128) * a.N);
+  a.u_slot_bytes = static_cast<uint32_t>(a.atoms) * CT * 128u;
+  const int q_bytes = round_up(a.atoms * a.N * 128, 1024);
+  const int ew = 8;
+  const int misc = round_up((kQ1Xch * ew * (a.N / 32) * 32) * 4 + 2 * kQ1Xch * 4, 16);
+  const int fixed = 1024 + q_bytes + misc + (2 * 16 + 2 * a.nts + 2) * 8 + 48;  // bars for up to 16 slots
+  a.nu = std::min(16, (kMaxSmem - fixed) / static_cast<int>(a.u_slot_bytes));
+  if (tune().nd > 0) a.nu = std::min(a.nu, tune().nd);
+  if (a.nu < 2) return false;
+  uint32_t off = 0;
+  a.off_q = off;
+  off += q_bytes;
+  a.off_u = off;
+  off += a.nu * a.u_slot_bytes;
+  a.off_misc = round_up(off, 16);
+  off = a.off_misc + misc;
+  a.off_bar = round_up(off, 16);
+  off = a.off_bar + (2 * a.nu + 2 * a.nts + 2) * 8 + 32;
+  smem = std::max(static_cast<int>(off) + 1024, kMinSmem);
+  return smem <= kMaxSmem;
+}
+
+template <int GQ, int CT>
+int launch_q1_t(const CUtensorMap& tq, const CUtensorMap& td, const Q1Args& a, int smem,
+                cudaStream_t stream) {
+  auto kern = maxsim_q1_kernel<GQ, 8, CT>;
+  static std::atomic<bool> cfg{false};
+  if (!cfg.load()) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess)
+      return FM_ERR_LAUNCH;
+    cfg.store(true);
+  }
+  const int sms = sm_count();
+  if (sms <= 0) return FM_ERR_NO_DEVICE;
+  kern<<<std::max(1, std::min(a.B, sms)), q1_threads(8), smem, stream>>>(tq, td, a);
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
+              int32_t* status, cudaStream_t stream) {
+  const int CT = tune().C == 256 ? 256 : 128;
+  Q1Args a{};
+  int smem = 0;
+  if (!plan_q1(s, CT, a, smem)) return FM_ERR_UNSUPPORTED;
+  a.lengths = lengths;
+  a.scores = scores;
+  a.status = status;
+  a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
+  a.dbg = tune().dbg;
+  CUtensorMap tq, td;
+  if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, 1, 64, a.N,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, s.Ld, s.B, 64, CT,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  if (a.N == 32)
+    return CT == 256 ? launch_q1_t<1, 256>(tq, td, a, smem, stream) : launch_q1_t<1, 128>(tq, td, a, smem, stream);
+  return CT == 256 ? launch_q1_t<2, 256>(tq, td, a, smem, stream) : launch_q1_t<2, 128>(tq, td, a, smem, stream);
 }
 
 }  // namespace

@@ -45,6 +45,11 @@
 #include <cuda_fp16.h>
 #include "fm_ptx.cuh"
 
+#ifdef FM_EXP_NOFENCE
+#define FM_EXP_FENCE()
+#else
+#define FM_EXP_FENCE() tc_fence_after()
+#endif
 namespace fm {
 
 enum FwdMode : int { MODE_DENSE = 0, MODE_SPARSE = 1, MODE_INT8 = 2 };
@@ -565,7 +570,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     ok = false;
                     break;
                   }
-                  tc_fence_after();
+                  FM_EXP_FENCE();
                   const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes);
                   const uint32_t tacc = tmem_base + tr.idx * a.ts_stride;
                   FM_PROF_T0(pm0);

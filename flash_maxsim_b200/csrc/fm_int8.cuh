@@ -410,8 +410,8 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         if (!ok) break;
         __threadfence_block();
       }
-#pragma unroll
       const int ew = warp - 2;
+#pragma unroll
       for (int g = 0; g < GQ; ++g) xch[((slot * EW + ew) * GQ + g) * 32 + lane] = acc[g];
       __syncwarp();
       int old = 0;

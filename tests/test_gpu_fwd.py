@@ -63,6 +63,12 @@ def test_golden_large_d(cuda):
     (4, 1024, 6, 1024, 128, False),   # visual-like, chunk groups + state
     (3, 64, 20, 700, 256, True),      # d=256: K split over two Q stages
     (2, 40, 10, 129, 320, True),      # d=320: odd atom count
+    # single short query (document chunk as the M operand)
+    (1, 40, 50, 513, 128, True),      # 64-column query, 3 chunks, ragged last chunk
+    (1, 8, 20, 1, 32, False),         # d=32 (half atom), one-token documents
+    (1, 64, 600, 256, 128, True),     # chunk-sized documents, many docs per CTA
+    (1, 33, 20, 257, 120, True),      # d=120, one token past a chunk
+    (1, 32, 2000, 77, 128, True),     # short documents, > 8 documents per exchange slot cycle
 ])
 def test_batched_vs_oracle(cuda, Nq, Lq, B, Ld, d, varlen):
     import flash_maxsim_b200 as fm
