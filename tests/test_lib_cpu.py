@@ -69,7 +69,7 @@ def test_plans_fit_shared_memory(args):
 
 def test_plan_groups_short_documents():
     from flash_maxsim_b200._lib import plan_info
-    assert plan_info(0, False, 100, 100000, 32, 300, 128)["gd"] >= 2
+    assert plan_info(0, False, 100, 100000, 32, 128, 128)["gd"] >= 2
     assert plan_info(0, False, 16, 4000, 1024, 1024, 128)["gd"] == 1
     assert plan_info(0, False, 1, 1000, 32, 300, 128)["q_resident"] == 1
 
