@@ -5,6 +5,7 @@ There is no fallback implementation.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 from pathlib import Path
@@ -93,8 +94,22 @@ def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device: torch.device) -> int:
+    """Handle of the current CUDA stream of `device` (what kernels launch on)."""
+    if _raw_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def on_device(device: torch.device):
+    """Context that makes `device` current for a launch (a no-op when it already is)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 _status: dict[int, torch.Tensor] = {}

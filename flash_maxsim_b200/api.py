@@ -78,7 +78,7 @@ def _fwd(Q3: torch.Tensor, D2: torch.Tensor, lengths, Nq, B, Lq, Ld, shared: boo
     if B == 0:
         return scores, argmax
     d = Q3.shape[-1]
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         rc = lib.fm_maxsim_fwd(
             Q3.data_ptr(), D2.data_ptr(), _lib.ptr(lengths), scores.data_ptr(),
             _lib.ptr(argmax), Nq, B, Lq, Ld, d, 1 if shared else 0,
@@ -181,7 +181,7 @@ class _FlashMaxSimFn(torch.autograd.Function):
         dev = Qh.device
         ws_bytes = int(lib.fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, dp))
         ws = torch.empty(max(ws_bytes, 0) // 4, device=dev, dtype=torch.float32) if ws_bytes > 0 else None
-        with torch.cuda.device(dev):
+        with _lib.on_device(dev):
             rc = lib.fm_maxsim_bwd(
                 Qh.data_ptr(), Dh.data_ptr(), argmax.data_ptr(), g.data_ptr(),
                 grad_Q.data_ptr(), grad_D.data_ptr(), Nq, B, Lq, Ld, dp,
@@ -251,7 +251,7 @@ def quantize_int8(D: torch.Tensor):
     mins = torch.empty(B, Ld, 1, device=D.device, dtype=torch.float16)
     rows = B * Ld
     if rows:
-        with torch.cuda.device(D.device):
+        with _lib.on_device(D.device):
             rc = lib.fm_quantize_int8(x.data_ptr(), _QDTYPE[x.dtype], u8.data_ptr(),
                                       scales.data_ptr(), mins.data_ptr(), rows, dp,
                                       _lib.stream_of(D.device))
@@ -296,7 +296,7 @@ def flash_maxsim_int8(Q: torch.Tensor, D_uint8: torch.Tensor, scales: torch.Tens
     if B == 0:
         return scores
     dev = Q.device
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         rc = lib.fm_maxsim_int8_fwd(Qh.data_ptr(), Du.data_ptr(), sc.data_ptr(), mn.data_ptr(),
                                     _lib.ptr(lengths), scores.data_ptr(), B, Lq, Ld,
                                     Qh.shape[-1], _lib.status_word(dev).data_ptr(),
@@ -338,7 +338,7 @@ def flash_maxsim_sparse(Q: torch.Tensor, D: torch.Tensor, indices: torch.Tensor,
     if B == 0:
         return scores
     dev = D.device
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         rc = lib.fm_maxsim_sparse_fwd(Qh.data_ptr(), Dh.data_ptr(), idx.data_ptr(),
                                       _lib.ptr(lengths), scores.data_ptr(), B, K, Lq, Ld,
                                       Qh.shape[-1], _lib.status_word(dev).data_ptr(),

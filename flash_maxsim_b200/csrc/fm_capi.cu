@@ -461,7 +461,17 @@ int launch_q1_t(const CUtensorMap& tq, const CUtensorMap& td, const Q1Args& a, i
   }
   const int sms = sm_count();
   if (sms <= 0) return FM_ERR_NO_DEVICE;
-  kern<<<std::max(1, std::min(a.B, sms)), q1_threads(8), smem, stream>>>(tq, td, a);
+  cudaLaunchConfig_t cfgl{};
+  cfgl.gridDim = dim3(std::max(1, std::min(a.B, sms)));
+  cfgl.blockDim = dim3(q1_threads(8));
+  cfgl.dynamicSmemBytes = smem;
+  cfgl.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfgl.attrs = attr;
+  cfgl.numAttrs = (tune().dbg & 128) ? 0 : 1;
+  if (cudaLaunchKernelEx(&cfgl, kern, tq, td, a) != cudaSuccess) return FM_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 

@@ -142,6 +142,10 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // the prologue above may overlap the previous kernel in the stream; inputs
+  // are read only after it has completed
+  grid_dep_wait();
+  grid_dep_launch();
   const uint32_t tmem_base = *tmem_slot;
   const int w0 = blockIdx.x, wstep = gridDim.x;
   const uint32_t ts_stride = NH * a.N;  // TMEM columns per slot
