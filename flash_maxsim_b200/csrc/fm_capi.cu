@@ -277,7 +277,7 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tq2, const CUtensorMap&
 
 bool q1_ok(const Shape& s);
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
-              int32_t* status, cudaStream_t stream);
+              const int32_t* sp_idx, int32_t* status, cudaStream_t stream);
 
 int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
                int32_t* argmax, const int32_t* sp_idx, const void* scales, const void* mins,
@@ -293,7 +293,7 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   const int64_t n_docs = s.shared ? s.B : static_cast<int64_t>(s.Nq) * s.B;
   if (n_docs > INT32_MAX || static_cast<int64_t>(s.Nq) * s.B > INT32_MAX) return FM_ERR_ARG;
 
-  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, status, stream);
+  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, sp_idx, status, stream);
 
   FwdArgs a{};
   int smem = 0;
@@ -416,8 +416,8 @@ int launch_int8_fast(const void* Q, const void* Du8, const void* scales, const v
 // Short-query path (fm_q1.cuh): one query of <= 64 rows and d <= 128 against
 // shared documents, the document chunk as the MMA's M operand.
 bool q1_ok(const Shape& s) {
-  return s.mode == MODE_DENSE && !s.argmax && s.Nq == 1 && s.Lq <= 64 && s.d <= 128 &&
-         !(tune().dbg & 8);
+  return (s.mode == MODE_DENSE || s.mode == MODE_SPARSE) && !s.argmax && s.Nq == 1 && s.Lq <= 64 &&
+         s.d <= 128 && !(tune().dbg & 8);
 }
 
 bool plan_q1(const Shape& s, int CT, Q1Args& a, int& smem) {
@@ -431,7 +431,7 @@ bool plan_q1(const Shape& s, int CT, Q1Args& a, int& smem) {
   a.u_slot_bytes = static_cast<uint32_t>(a.atoms) * CT * 128u;
   const int q_bytes = round_up(a.atoms * a.N * 128, 1024);
   const int ew = 8;
-  const int misc = round_up((kQ1Xch * ew * (a.N / 32) * 32) * 4 + 2 * kQ1Xch * 4, 16);
+  const int misc = round_up((kQ1Xch * ew * (a.N / 32) * 32) * 4 + 2 * kQ1Xch * 4 + ew * a.N * 4, 16);
   const int fixed = 1024 + q_bytes + misc + (2 * 16 + 2 * a.nts + 2) * 8 + 48;  // bars for up to 16 slots
   a.nu = std::min(16, (kMaxSmem - fixed) / static_cast<int>(a.u_slot_bytes));
   if (tune().nd > 0) a.nu = std::min(a.nu, tune().nd);
@@ -476,7 +476,7 @@ int launch_q1_t(const CUtensorMap& tq, const CUtensorMap& td, const Q1Args& a, i
 }
 
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
-              int32_t* status, cudaStream_t stream) {
+              const int32_t* sp_idx, int32_t* status, cudaStream_t stream) {
   const int CT = tune().C == 256 ? 256 : 128;
   Q1Args a{};
   int smem = 0;
@@ -486,6 +486,9 @@ int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengt
   a.status = status;
   a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
   a.dbg = tune().dbg;
+  a.sparse = s.mode == MODE_SPARSE ? 1 : 0;
+  a.sp_idx = sp_idx;
+  a.K = s.mode == MODE_SPARSE ? s.K : 0;
   CUtensorMap tq, td;
   if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, 1, 64, a.N,
                    CU_TENSOR_MAP_SWIZZLE_128B))

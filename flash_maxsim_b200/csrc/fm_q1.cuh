@@ -50,6 +50,9 @@ struct Q1Args {
   int nu;                  // document ring slots
   int nts;                 // TMEM slots (CT / 128 halves of N columns each)
   uint32_t off_q, off_u, off_misc, off_bar, u_slot_bytes;
+  const int32_t* sp_idx;    // sparse scoring: [B, K] query-row indices (negative ones wrap), else null
+  int K;                   // indices per document (sparse scoring)
+  int sparse;              // 1: score[b] = sum_k rowmax[idx[b, k]]
   int dbg;                 // tuning experiments only: bit 0 skip epilogue math, bit 1 skip MMAs
 };
 
@@ -112,6 +115,7 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
   float* xch = reinterpret_cast<float*>(smem + a.off_misc);        // [kQ1Xch docs][EW warps][GQ][32]
   int* cnt = reinterpret_cast<int*>(xch + kQ1Xch * EW * GQ * 32);  // [kQ1Xch] arrivals
   volatile int* done = cnt + kQ1Xch;                               // [kQ1Xch] combined generations
+  float* rowmax_s = reinterpret_cast<float*>(cnt + 2 * kQ1Xch);   // [EW][32 GQ] sparse scoring
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.nu; ++i) {
@@ -324,11 +328,34 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
       if (old == EW - 1) {
         __threadfence_block();
         float tot = 0.f;
+        float* rm = rowmax_s + ew * 32 * GQ;
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
           float mm = -INFINITY;
           for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
           tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
+          rm[g * 32 + lane] = mm;
+        }
+        if (a.sparse) {
+          // score = sum over the document's K query-row indices of their row maxima
+          // (flash_maxsim/flash_maxsim_sparse.py:60-80); an empty document scores
+          // 0 when K == 0 and -inf otherwise
+          __syncwarp();
+          tot = 0.f;
+          if (len == 0) {
+            tot = (a.K == 0 || lane != 0) ? 0.f : -INFINITY;
+          } else {
+            const int32_t* ip = a.sp_idx + static_cast<size_t>(b) * a.K;
+            for (int k = lane; k < a.K; k += 32) {
+              int q = __ldg(ip + k);
+              if (q < 0) q += a.Lq;
+              if (q < 0 || q >= a.Lq) {
+                record_status(a.status, FM_ERR_BAD_INDEX);
+                continue;
+              }
+              tot += rm[q];
+            }
+          }
         }
         tot = warp_sum(tot);
         if (lane == 0) {

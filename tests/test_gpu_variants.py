@@ -98,7 +98,7 @@ def test_sparse_golden(cuda):
     close(got.cpu(), g["scores"])
 
 
-@pytest.mark.parametrize("Lq,K,B,Ld", [(32, 8, 100, 300), (32, 32, 50, 64), (100, 37, 20, 500),
+@pytest.mark.parametrize("Lq,K,B,Ld", [(32, 8, 100, 300), (32, 32, 50, 64), (100, 37, 20, 500), (64, 70, 30, 129), (32, 0, 12, 40),
                                        (16, 3, 40, 17)])
 def test_sparse_vs_oracle(cuda, Lq, K, B, Ld):
     import flash_maxsim_b200 as fm
