@@ -17,6 +17,7 @@
 #include "fm_fwd.cuh"
 #include "fm_int8.cuh"
 #include "fm_q1.cuh"
+#include "fm_flat.cuh"
 
 // Scratch for fm_maxsim_bwd_noalloc: the dQ partial sums live here instead of
 // in caller-provided memory.  Every device that loads this library keeps
@@ -80,7 +81,7 @@ bool make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* 
 // Optional plan overrides for tuning sweeps, e.g.
 // FLASH_MAXSIM_TUNE="nd=3,nq=3,gd=2" (read once per process).
 struct Tune {
-  int nd = 0, nq = 0, G = 0, C = 0, dbg = 0, gd = 0;
+  int nd = 0, nq = 0, G = 0, C = 0, dbg = 0, gd = 0, flat = 0;
 };
 const Tune& tune() {
   static Tune t;
@@ -99,6 +100,7 @@ const Tune& tune() {
       if (!std::strcmp(key, "C")) t.C = v;
       if (!std::strcmp(key, "dbg")) t.dbg = v;
       if (!std::strcmp(key, "gd")) t.gd = v;
+      if (!std::strcmp(key, "flat")) t.flat = v;
       p += n;
       if (*p == ',') ++p;
     }
@@ -276,6 +278,9 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tq2, const CUtensorMap&
 }
 
 bool q1_ok(const Shape& s);
+bool flat_ok(const Shape& s, const int32_t* lengths);
+int launch_flat(const Shape& s, const void* Q, const void* D, float* scores, int32_t* status,
+                cudaStream_t stream);
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
               const int32_t* sp_idx, int32_t* status, cudaStream_t stream);
 
@@ -294,6 +299,7 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   if (n_docs > INT32_MAX || static_cast<int64_t>(s.Nq) * s.B > INT32_MAX) return FM_ERR_ARG;
 
   if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, sp_idx, status, stream);
+  if (flat_ok(s, lengths)) return launch_flat(s, Q, D, scores, status, stream);
 
   FwdArgs a{};
   int smem = 0;
@@ -499,6 +505,83 @@ int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengt
   if (a.N == 32)
     return CT == 256 ? launch_q1_t<1, 256>(tq, td, a, smem, stream) : launch_q1_t<1, 128>(tq, td, a, smem, stream);
   return CT == 256 ? launch_q1_t<2, 256>(tq, td, a, smem, stream) : launch_q1_t<2, 128>(tq, td, a, smem, stream);
+}
+
+// Flat-token path (fm_flat.cuh): shared documents of one length (no lengths
+// array, Ld >= 128), whole 32-row query row groups, >= 128 query rows, d <= 128.
+bool flat_ok(const Shape& s, const int32_t* lengths) {
+  if (s.mode != MODE_DENSE || s.argmax || !s.shared || lengths != nullptr) return false;
+  if (s.Lq % 32 != 0 || s.Nq * s.Lq < 128 || s.d > 128 || s.Lq / 32 > 4 * kFlatMaxJb) return false;
+  // measured slower than the per-document kernel on B200 so far (the epilogue
+  // cannot drain a 192-column chunk within one chunk's MMA time): opt-in only
+  if (s.Ld < 128 || !tune().flat) return false;
+  return static_cast<int64_t>(s.B) * s.Ld + 2 * kFlatCT < (static_cast<int64_t>(1) << 31);
+}
+
+bool plan_flat(const Shape& s, FlatArgs& a, int& smem) {
+  a.B = s.B;
+  a.Ld = s.Ld;
+  a.Nq = s.Nq;
+  a.Lq = s.Lq;
+  a.d = s.d;
+  a.atoms = cdiv(s.d, 64);
+  a.nd = 3;
+  a.Gq = s.Lq / 32;
+  a.R = s.Nq * a.Gq;
+  a.span_rg = a.R <= 4 * kFlatMaxJb ? a.R : (4 * kFlatMaxJb / a.Gq) * a.Gq;
+  a.d_slot_bytes = static_cast<uint32_t>(a.atoms) * kFlatCT * 128u;
+  uint32_t off = 0;
+  a.off_q = off;
+  off += 2 * 32768u;
+  a.off_d = off;
+  off += a.nd * a.d_slot_bytes;
+  a.off_rows = off;
+  off += 2 * kFlatDocSlots * 128 * 4;
+  a.off_xch = off;
+  off += kFlatXch * 4 * kFlatSeg * 32 * 4;
+  a.off_bar = off;
+  off += (2 * a.nd + 4 + 2 * kFlatTS + 4 * kFlatXch + 3) * 8 + 16;
+  smem = std::max(static_cast<int>(off) + 1024, kMinSmem);
+  return smem <= kMaxSmem;
+}
+
+int launch_flat(const Shape& s, const void* Q, const void* D, float* scores, int32_t* status,
+                cudaStream_t stream) {
+  FlatArgs a{};
+  int smem = 0;
+  if (!plan_flat(s, a, smem)) return FM_ERR_UNSUPPORTED;
+  a.scores = scores;
+  a.status = status;
+  a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
+  a.dbg = tune().dbg;
+  CUtensorMap tq, td;
+  if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, static_cast<uint64_t>(s.Nq) * s.Lq, 1, 64,
+                   128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, static_cast<uint64_t>(s.B) * s.Ld, 1, 64,
+                   kFlatCT, CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  static std::atomic<bool> cfg{false};
+  if (!cfg.load()) {
+    if (cudaFuncSetAttribute(maxsim_flat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+        cudaSuccess)
+      return FM_ERR_LAUNCH;
+    cfg.store(true);
+  }
+  const int sms = sm_count();
+  if (sms <= 0) return FM_ERR_NO_DEVICE;
+  cudaLaunchConfig_t cfgl{};
+  cfgl.gridDim = dim3(std::max(1, std::min(s.B, sms)));
+  cfgl.blockDim = dim3(kFlatThreads);
+  cfgl.dynamicSmemBytes = smem;
+  cfgl.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfgl.attrs = attr;
+  cfgl.numAttrs = (tune().dbg & 128) ? 0 : 1;
+  if (cudaLaunchKernelEx(&cfgl, maxsim_flat_kernel, tq, td, a) != cudaSuccess) return FM_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
 }  // namespace
@@ -722,6 +805,19 @@ int fm_prof_read(unsigned long long* out, int reset) {
   if (reset) {
     const unsigned long long z[32] = {0};
     if (cudaMemcpyToSymbol(g_fm_prof, z, sizeof(z)) != cudaSuccess) return FM_ERR_LAUNCH;
+  }
+  return FM_OK;
+}
+#endif
+
+#ifdef FM_TRACE
+int fm_trace_read(unsigned long long* out, int reset) {
+  if (cudaMemcpyFromSymbol(out, g_fm_trace, sizeof(unsigned long long) * 8 * 4096) != cudaSuccess)
+    return FM_ERR_LAUNCH;
+  if (reset) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fm_trace) != cudaSuccess) return FM_ERR_LAUNCH;
+    if (cudaMemset(p, 0, sizeof(unsigned long long) * 8 * 4096) != cudaSuccess) return FM_ERR_LAUNCH;
   }
   return FM_OK;
 }

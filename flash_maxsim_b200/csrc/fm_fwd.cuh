@@ -421,6 +421,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       Ring r;
       int issued = 0;
       bool ok = true;
+      FM_TR_DECL;
       for (int w = w0; w < a.n_work && ok; w += wstep) {
         const Item it = make_item(a, w);
         for (int s0 = it.rg_lo; s0 < it.rg_hi && ok; s0 += it.span) {
@@ -437,15 +438,18 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
               for (int c = cb; c < ce; ++c) {
                 const uint32_t empty = (MODE == MODE_INT8) ? bars.u_empty(r.idx) : bars.d_empty(r.idx);
                 const uint32_t full = (MODE == MODE_INT8) ? bars.u_full(r.idx) : bars.d_full(r.idx);
+                FM_TR(4, 1);
                 if (!mbar_wait(empty, r.phase ^ 1u, ctl,
                                MODE == MODE_INT8 ? FM_ERR_TIMEOUT_UEMPTY : FM_ERR_TIMEOUT_DEMPTY)) {
                   ok = false;
                   break;
                 }
+                FM_TR(4, 2);
                 mbar_expect_tx(full, tx);
                 const uint32_t dst = ring_base + r.idx * slot_bytes;
                 for (int at = 0; at < a.d_atoms_real; ++at)
                   tma_load_3d(dst + at * atom_bytes, &tmap_d, at * 64, c * a.C, doc, full, pol);
+                FM_TR(4, 3);
                 r.next(nslots);
                 ++issued;
               }
@@ -470,6 +474,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       Ring r;
       int issued = 0;
       bool ok = true;
+      FM_TR_DECL;
       for (int w = w0; w < a.n_work && ok; w += wstep) {
         const Item it = make_item(a, w);
         if (it.nch_total == 0) continue;
@@ -480,10 +485,12 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
             for (int jb = 0; jb < nmb && ok; ++jb) {
               for (int ks = 0; ks < a.nk; ++ks) {
                 if (a.q_resident && issued > 0) break;
+                FM_TR(3, 1);
                 if (!mbar_wait(bars.q_empty(r.idx), r.phase ^ 1u, ctl, FM_ERR_TIMEOUT_QEMPTY)) {
                   ok = false;
                   break;
                 }
+                FM_TR(3, 2);
                 const int at_hi = min(a.kq_atoms, a.d_atoms_real - ks * a.kq_atoms);
                 const uint32_t dst = sbase + a.off_q + r.idx * a.q_stage_bytes;
                 const uint32_t full = bars.q_full(r.idx);
@@ -534,6 +541,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       const bool skip_mma = (a.dbg & 2) != 0;
       Ring dr, qr, tr;
       bool ok = true;
+      FM_TR_DECL;
       for (int w = w0; w < a.n_work && ok; w += wstep) {
         const Item it = make_item(a, w);
         if (it.nch_total == 0) continue;
@@ -544,6 +552,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
             const int cn = group_chunks(a, it, g);
             {
               Ring r = dr;
+              FM_TR(0, 8);
               for (int c = 0; c < cn; ++c) {
                 if (!mbar_wait(bars.d_full(r.idx), r.phase, ctl, FM_ERR_TIMEOUT_DFULL)) {
                   ok = false;
@@ -551,6 +560,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 }
                 r.next(a.nd);
               }
+              FM_TR(0, 9);
             }
             if (!ok) break;
             tc_fence_after();
@@ -558,18 +568,24 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
               if (a.nk == 1) {
                 const int qslot = a.q_resident ? 0 : qr.idx;
                 const uint32_t qph = a.q_resident ? 0u : qr.phase;
-                if (!mbar_wait(bars.q_full(qslot), qph, ctl, FM_ERR_TIMEOUT_QFULL)) {
+                FM_TR(0, 5);
+                if (!((a.dbg & 1024) && qr.phase) && !((a.dbg & 256) && mbar_test_wait(bars.q_full(qslot), qph)) &&
+                    !mbar_wait(bars.q_full(qslot), qph, ctl, FM_ERR_TIMEOUT_QFULL)) {
                   ok = false;
                   break;
                 }
+                FM_TR(0, 6);
                 tc_fence_after();
                 const uint64_t adesc = smem_desc_sw128(sbase + a.off_q + qslot * a.q_stage_bytes);
                 Ring r = dr;
                 for (int c = 0; c < cn; ++c) {
-                  if (!mbar_wait(bars.t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
+                  FM_TR(0, 1);
+                  if (!(a.dbg & 512) && !((a.dbg & 256) && mbar_test_wait(bars.t_empty(tr.idx), tr.phase ^ 1u)) &&
+                      !mbar_wait(bars.t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
                     ok = false;
                     break;
                   }
+                  FM_TR(0, 2);
                   FM_EXP_FENCE();
                   const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes);
                   const uint32_t tacc = tmem_base + tr.idx * a.ts_stride;
@@ -586,7 +602,9 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     }
                   }
                   FM_PROF_ADD(20, pm0);
+                  FM_TR(0, 3);
                   tc_commit(bars.t_full(tr.idx));
+                  FM_TR(0, 4);
                   tr.next(a.nts);
                   r.next(a.nd);
                 }
@@ -595,6 +613,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                   tc_commit(bars.q_empty(qr.idx));
                   qr.next(a.nq);
                 }
+                FM_TR(0, 7);
               } else {
                 // K split over several Q stages (single-document items only):
                 // every chunk slot of this M-block stays live until the last stage.
@@ -704,6 +723,8 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
     }
     Ring tr, er;
     bool ok = true;
+    FM_TR_DECL;
+    const int tch = warp == kEpiWarp0 ? 1 : (warp == kEpiWarp1 ? 2 : 7);
     for (int w = w0; w < a.n_work && ok; w += wstep) {
       const Item it = make_item(a, w);
       if (it.nch_total == 0) {
@@ -761,10 +782,12 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                   scs = reinterpret_cast<const float2*>(smem + a.off_sc) + sr.idx * a.C;
                   sr.next(a.nd);
                 }
+                FM_TR(tch, 1);
                 if (!mbar_wait(bars.t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) {
                   ok = false;
                   break;
                 }
+                FM_TR(tch, 2);
                 tc_fence_after();
                 FM_PROF_T0(pe0);
                 if (MODE != MODE_INT8 && !ARGMAX && rep == 1) {
@@ -805,6 +828,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 FM_PROF_ADD(22 + sub, pe0);
                 tc_fence_before();
                 __syncwarp();
+                FM_TR(tch, 3);
                 if (lane == 0) mbar_arrive(bars.t_empty(tr.idx));
                 tr.next(a.nts);
               }
@@ -815,7 +839,9 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                   xp_m[xbuf * 128 + sub * 32 + lane] = acc.m;
                   if (ARGMAX) xp_i[xbuf * 128 + sub * 32 + lane] = acc.idx;
                 }
+                FM_TR(tch, 5);
                 named_bar_sync(2 + sub, 64);
+                FM_TR(tch, 6);
                 if (half == 0)
                   acc.merge(xp_m[xbuf * 128 + sub * 32 + lane], ARGMAX ? xp_i[xbuf * 128 + sub * 32 + lane] : 0);
                 xbuf ^= 1;

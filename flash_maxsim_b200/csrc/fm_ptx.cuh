@@ -66,6 +66,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared control block of one CTA: an abort flag in shared memory that every
 // role polls while it waits, the caller's global status word and the wait
 // limit.  The first wait that runs out of time records its code, raises the
@@ -98,6 +111,23 @@ __device__ unsigned long long g_fm_prof[32];
   } while (0)
 #endif
 
+#ifdef FM_TRACE
+// Tracing builds only (never shipped): timestamped events of the lane-0
+// threads of CTA 0, one channel of 4096 entries per role, (clock64 << 8) | code.
+__device__ unsigned long long g_fm_trace[8 * 4096];
+#define FM_TR_DECL int tr_n_ = 0
+#define FM_TR(ch, code)                                                                          \
+  do {                                                                                           \
+    if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && tr_n_ < 4096)                              \
+      g_fm_trace[(ch) * 4096 + tr_n_++] = (static_cast<unsigned long long>(clock64()) << 8) | (code); \
+  } while (0)
+#else
+#define FM_TR_DECL
+#define FM_TR(ch, code) \
+  do {                  \
+  } while (0)
+#endif
+
 // Bounded wait on an mbarrier phase. Returns false when the CTA is aborting
 // (this wait ran out of time, or another role's did).
 __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
@@ -105,6 +135,9 @@ __device__ __forceinline__ bool mbar_wait_impl(uint32_t bar, uint32_t parity, co
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
+#ifdef FM_WAIT_SLEEP
+    __nanosleep(FM_WAIT_SLEEP);
+#endif
     if (mbar_try_wait(bar, parity)) return true;
     if (*ctl.abort_flag) return false;
     if (globaltimer_ns() - t0 > ctl.timeout_ns) {
@@ -262,6 +295,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
       : "r"(taddr));
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One fp32 column of 32 lanes to / from TMEM (per-row scratch values).
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v))
+               : "memory");
+}
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+  return __uint_as_float(r);
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() {

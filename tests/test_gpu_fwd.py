@@ -69,6 +69,16 @@ def test_golden_large_d(cuda):
     (1, 64, 600, 256, 128, True),     # chunk-sized documents, many docs per CTA
     (1, 33, 20, 257, 120, True),      # d=120, one token past a chunk
     (1, 32, 2000, 77, 128, True),     # short documents, > 8 documents per exchange slot cycle
+    # flat token stream (no lengths, whole row groups, >= 128 query rows)
+    (4, 32, 300, 300, 128, False),    # documents straddle 224-token chunks
+    (5, 64, 77, 150, 128, False),     # several documents end in one item
+    (4, 32, 97, 128, 128, False),     # shortest flat documents: two ends in one chunk
+    (4, 32, 61, 130, 128, False),
+    (2, 96, 200, 257, 96, False),     # d=96, odd Ld
+    (3, 64, 50, 200, 64, False),      # one K atom, 256-token chunks
+    (40, 128, 20, 300, 128, False),   # 160 row groups: two query spans
+    (16, 1024, 7, 1024, 128, False),  # long queries, spans of 4 queries
+    (100, 32, 1000, 300, 128, False), # config-2 shapes, few documents per CTA
 ])
 def test_batched_vs_oracle(cuda, Nq, Lq, B, Ld, d, varlen):
     import flash_maxsim_b200 as fm
