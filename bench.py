@@ -477,17 +477,20 @@ def cpu_baseline(cfg: str, seconds: float):
     if kind == "int8":
         u8, s, m = O.quantize_int8(D)
         D = O.dequantize_int8(u8, s, m)
-    t0 = time.perf_counter()
-    done = 0
-    while True:
-        for n in range(nq):
-            O.maxsim(Q[n], D)
-        done += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
+    # every host thread, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1)
+    from threadpoolctl import threadpool_limits
+    threads = os.cpu_count() or 1
+    with threadpool_limits(limits=threads):
+        t0 = time.perf_counter()
+        done = 0
+        while True:
+            for n in range(nq):
+                O.maxsim(Q[n], D)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
     units = done * n_docs * (nq if kind in ("batched", "train") else 1)
-    threads = os.environ.get("OMP_NUM_THREADS") or str(os.cpu_count())
     unit_name = "query-doc scores/s" if kind in ("batched", "train") else "docs/s"
     return {"value": round(units / el, 1), "unit": unit_name, "cores": int(threads), "kind": "port",
             "sample": f"{nq} queries x {n_docs} docs of the {cfg} shapes, repeated for {el:.1f} s "
