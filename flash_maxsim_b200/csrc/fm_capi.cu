@@ -354,7 +354,7 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   a.d = d;
   const int gq = cdiv(Lq, 32);
   a.N = 64 * gq;
-  a.nts = 512 / (2 * a.N);  // a slot holds the two 128-token halves of a chunk
+  a.nts = std::min(16, 512 / (kI8Halves * a.N));  // a slot holds the 128-token halves of a chunk
   a.atoms = cdiv(d, 128);
   a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
   a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);

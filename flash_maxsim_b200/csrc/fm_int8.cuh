@@ -39,8 +39,12 @@ namespace fm {
 // two warps + 4 or 8 epilogue warps (8: two per TMEM lane quarter taking
 // alternate chunks, so every scheduler has two independent epilogue warps)
 __host__ __device__ constexpr int i8_threads(int epi_warps) { return (2 + epi_warps) * 32; }
-constexpr int kI8Tokens = 256;  // tokens per chunk (one TMA box)
-constexpr int kI8Half = 128;    // tokens per MMA (M); a chunk is two M blocks
+#ifndef FM_I8_TOKENS
+#define FM_I8_TOKENS 256
+#endif
+constexpr int kI8Tokens = FM_I8_TOKENS;  // tokens per chunk (one TMA box)
+constexpr int kI8Half = 128;             // tokens per MMA (M)
+constexpr int kI8Halves = kI8Tokens / kI8Half;  // M blocks per chunk
 constexpr int kI8Xch = 8;       // per-document exchange slots of the epilogue
 
 struct Int8Args {
@@ -224,15 +228,18 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
       bool ok = mbar_wait(q_ready, 0, ctl, FM_ERR_TIMEOUT_QFULL);
       tc_fence_after();
       for (int b = w0; b < a.B && ok; b += wstep) {
-        const int nch = (i8_len(a, b) + kI8Tokens - 1) / kI8Tokens;
+        const int len = i8_len(a, b);
+        const int nch = (len + kI8Tokens - 1) / kI8Tokens;
         for (int c = 0; c < nch; ++c) {
+          // a half with no valid token is neither multiplied nor read by the epilogue
+          const int nhalf = min(kI8Halves, (len - c * kI8Tokens + kI8Half - 1) / kI8Half);
           if (!mbar_wait(u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
           if (!mbar_wait(t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) { ok = false; break; }
           tc_fence_after();
           FM_PROF_T0(pm0);
           const uint64_t au = smem_desc_sw128(sbase + a.off_u + ur.idx * a.u_slot_bytes);
-          const uint32_t tacc = tmem_base + tr.idx * 2 * a.N;
-          for (int hb = 0; hb < 2; ++hb) {  // rows [128 hb, 128 hb + 128) of the chunk
+          const uint32_t tacc = tmem_base + tr.idx * kI8Halves * a.N;
+          for (int hb = 0; hb < nhalf; ++hb) {  // rows [128 hb, 128 hb + 128) of the chunk
             const uint64_t ah = au + hb * (kI8Half * 128u >> 4);
             for (int at = 0; at < a.atoms && !(a.dbg & 2); ++at) {
 #pragma unroll
@@ -317,7 +324,10 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
     float qsm[32 * GQ];
 #pragma unroll
     for (int j = 0; j < 32 * GQ; ++j) qsm[j] = qsum_s[j];
-    const int half = (EW == 8) ? (warp - 2) / 4 : 0;  // which alternate chunks this warp takes
+    // EW == 8: the two warps of a lane quarter take alternate documents, so the
+    // four warps of one set reduce a whole document (fewer lane reductions)
+    const int half = (EW == 8) ? (warp - 2) / 4 : 0;
+    constexpr int EWD = EW == 8 ? 4 : EW;  // warps that score one document
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     const int tok_in_chunk = sub * 32 + lane;
     Ring ur, tr;
@@ -331,8 +341,9 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
       float rmax[32 * GQ];
 #pragma unroll
       for (int j = 0; j < 32 * GQ; ++j) rmax[j] = -INFINITY;
+      const bool mine = EW != 8 || (dloc & 1) == half;
       for (int c = 0; c < nch; ++c, ++kglob) {
-        if (EW == 8 && (kglob & 1) != half) {  // the other warp of this lane quarter takes it
+        if (!mine) {  // the other warp of this lane quarter takes the document
           tr.next(a.nts);
           ur.next(a.nu);
           continue;
@@ -347,11 +358,11 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         const uint8_t* stage = smem + a.off_sc + ur.idx * a.sc_slot_bytes;
         const bool full = (c + 1) * kI8Tokens <= len;  // whole chunk valid (warp-uniform)
 #pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
+        for (int hb = 0; hb < kI8Halves; ++hb) {
           const int tic = hb * kI8Half + tok_in_chunk;
           const bool valid = c * kI8Tokens + tic < len;
           if (!full && !__any_sync(0xffffffffu, valid)) continue;
-          const uint32_t th = tmem_base + lane_base + tr.idx * 2 * a.N + hb * a.N;
+          const uint32_t th = tmem_base + lane_base + tr.idx * kI8Halves * a.N + hb * a.N;
           const int sh = static_cast<int>((byte0 & 15) >> 1) + tic;
           const float s_t = __half2float(reinterpret_cast<const __half*>(stage)[sh]);
           const float m_t = __half2float(reinterpret_cast<const __half*>(stage + a.sc_slot_bytes / 2)[sh]);
@@ -383,6 +394,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         ur.next(a.nu);
       }
       if (!ok) break;
+      if (!mine) continue;
       float acc[GQ];
 #pragma unroll
       for (int g = 0; g < GQ; ++g) {
@@ -410,7 +422,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         if (!ok) break;
         __threadfence_block();
       }
-      const int ew = warp - 2;
+      const int ew = (warp - 2) % EWD;
 #pragma unroll
       for (int g = 0; g < GQ; ++g) xch[((slot * EW + ew) * GQ + g) * 32 + lane] = acc[g];
       __syncwarp();
@@ -420,13 +432,13 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         old = atomicAdd(&cnt[slot], 1);
       }
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == EW - 1) {
+      if (old == EWD - 1) {
         __threadfence_block();
         float tot = 0.f;
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
           float mm = -INFINITY;
-          for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
+          for (int w = 0; w < EWD; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
           tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
         }
         tot = warp_sum(tot);
