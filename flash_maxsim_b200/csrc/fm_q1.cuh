@@ -235,7 +235,10 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
   } else {
     // ===================== epilogue =====================
     const int sub = warp & 3;  // TMEM lane quarter = tokens [32 sub, 32 sub + 32) of each half
-    const int half = (EW == 8) ? (warp - 2) / 4 : 0;  // which alternate chunks this warp takes
+    // EW == 8: the two warps of a lane quarter take alternate documents, so the
+    // four warps of one set reduce a whole document
+    const int half = (EW == 8) ? (warp - 2) / 4 : 0;
+    constexpr int EWD = EW == 8 ? 4 : EW;  // warps that score one document
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     const int tok_in_half = sub * 32 + lane;
     Ring tr;
@@ -249,8 +252,9 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
       float rmax[32 * GQ];
 #pragma unroll
       for (int j = 0; j < 32 * GQ; ++j) rmax[j] = -INFINITY;
+      const bool mine = EW != 8 || (dloc & 1) == half;
       for (int c = 0; c < nch; ++c, ++kglob) {
-        if (EW == 8 && (kglob & 1) != half) {  // the other warp of this lane quarter takes it
+        if (!mine) {  // the other warp of this lane quarter takes the document
           tr.next(a.nts);
           continue;
         }
@@ -288,6 +292,7 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
         tr.next(a.nts);
       }
       if (!ok) break;
+      if (!mine) continue;
       float acc[GQ];
 #pragma unroll
       for (int g = 0; g < GQ; ++g) {
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
         if (!ok) break;
         __threadfence_block();
       }
-      const int ew = warp - 2;
+      const int ew = (warp - 2) % EWD;
 #pragma unroll
       for (int g = 0; g < GQ; ++g) xch[((slot * EW + ew) * GQ + g) * 32 + lane] = acc[g];
       __syncwarp();
@@ -325,14 +330,14 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
         old = atomicAdd(&cnt[slot], 1);
       }
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == EW - 1) {
+      if (old == EWD - 1) {
         __threadfence_block();
         float tot = 0.f;
         float* rm = rowmax_s + ew * 32 * GQ;
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
           float mm = -INFINITY;
-          for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
+          for (int w = 0; w < EWD; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
           tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
           rm[g * 32 + lane] = mm;
         }
