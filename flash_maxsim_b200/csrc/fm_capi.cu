@@ -158,6 +158,7 @@ bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
   a.q_resident = (s.shared && a.R <= 4 && a.nk == 1) ? 1 : 0;
   a.q_flat = (s.Lq % 32 == 0) ? 1 : 0;
   a.dbg = tune().dbg;
+  a.mma2 = (!int8 && a.nk == 1 && a.nts >= 2 && !(tune().dbg & 4096)) ? 1 : 0;
   a.q_stage_bytes = a.kq_atoms * 16384u;
   a.d_slot_bytes = static_cast<uint32_t>(a.d_atoms) * a.C * 128u;
   a.u_slot_bytes = int8 ? static_cast<uint32_t>(a.d_atoms) * a.C * 64u : 0u;
@@ -355,6 +356,7 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   const int gq = cdiv(Lq, 32);
   a.N = 64 * gq;
   a.nts = std::min(16, 512 / (kI8Halves * a.N));  // a slot holds the 128-token halves of a chunk
+  if (a.nts % 2) return false;  // the two warps of a lane quarter own alternate slots
   a.atoms = cdiv(d, 128);
   a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
   a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);
@@ -434,6 +436,7 @@ bool plan_q1(const Shape& s, int CT, Q1Args& a, int& smem) {
   a.N = 32 * cdiv(s.Lq, 32);
   a.atoms = cdiv(s.d, 64);
   a.nts = 512 / ((CT / 128) * a.N);
+  if (a.nts % 2) return false;  // the two warps of a lane quarter own alternate slots
   a.u_slot_bytes = static_cast<uint32_t>(a.atoms) * CT * 128u;
   const int q_bytes = round_up(a.atoms * a.N * 128, 1024);
   const int ew = 8;

@@ -58,7 +58,8 @@ constexpr int kEpiWarp0 = 2;   // epilogue warps 2..5
 constexpr int kQProdWarp = 6;
 constexpr int kEpiWarp1 = 7;   // second epilogue set 7..10 (fp16 modes): odd query blocks
 constexpr int kConvWarp0 = 7;  // INT8 converters 7..10
-constexpr int kThreadsF16 = 11 * 32;
+constexpr int kMmaWarp2 = 11;  // second MMA issuer (fp16 modes, K in one query stage)
+constexpr int kThreadsF16 = 12 * 32;
 constexpr int kThreadsI8 = 11 * 32;
 constexpr int kMaxGroupDocs = 8;
 
@@ -91,6 +92,7 @@ struct FwdArgs {
   int rep;                   // lane-quarter replication (1, 2 or 4)
   int q_resident;            // Q loaded once for the whole launch
   int q_flat;                // Lq % 32 == 0: an M-block is 128 consecutive rows of Q
+  int mma2;                  // 1: two MMA issuers (warps 1 and 11) take alternate chunks
   int dbg;                   // tuning experiments only: bit 0 skip epilogue reads, bit 1 skip MMAs
   int nts;                   // TMEM accumulator slots
   int ts_stride;             // TMEM columns per slot
@@ -354,11 +356,11 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.nq; ++i) {
       mbar_init(bars.q_full(i), 1);
-      mbar_init(bars.q_empty(i), 1);
+      mbar_init(bars.q_empty(i), a.mma2 ? 2 : 1);  // a commit from every MMA issuer
     }
     for (int i = 0; i < a.nd; ++i) {
       mbar_init(bars.d_full(i), MODE == MODE_INT8 ? 128 : 1);
-      mbar_init(bars.d_empty(i), 1);
+      mbar_init(bars.d_empty(i), a.mma2 ? 2 : 1);
     }
     for (int i = 0; i < a.nts; ++i) {
       mbar_init(bars.t_full(i), 1);
@@ -372,7 +374,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       }
       for (int i = 0; i < a.nd; ++i) mbar_init(bars.s_empty(i), 4);
     }
-    mbar_init(bars.drain(), 1);
+    mbar_init(bars.drain(), a.mma2 ? 2 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -532,9 +534,14 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
         drain_wait(bars.q_full(r.idx), r.phase, a);
       }
     }
-  } else if (warp == 1) {
-    // ===================== MMA issuer =====================
+  } else if (warp == 1 || (MODE != MODE_INT8 && warp == kMmaWarp2 && a.mma2)) {
+    // ===================== MMA issuer(s) =====================
+    // With a.mma2 two threads (warps 1 and 11) issue: each owns alternate TMEM
+    // slots (and so the chunks that land in them), so one issues while the
+    // other waits or commits; both follow the same ring positions and both
+    // commit the query stage, document slot and drain barriers (counts of 2).
     if (lane == 0) {
+      const int me = warp == 1 ? 0 : 1;
       const uint32_t idesc = idesc_f16_f32(128, a.C);
       const int ksteps = a.kq_atoms * 4;  // K=16 steps per Q stage (4 or 8)
       const uint32_t b_atom = a.C * 8u;    // one K atom of a D slot, in 16-byte units
@@ -579,6 +586,14 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 const uint64_t adesc = smem_desc_sw128(sbase + a.off_q + qslot * a.q_stage_bytes);
                 Ring r = dr;
                 for (int c = 0; c < cn; ++c) {
+                  // slots alternate between the issuers: every use of a slot is issued
+                  // (and its release awaited) by the same thread, so no issuer ever
+                  // waits on a slot barrier more than one phase ahead
+                  if (a.mma2 && (tr.idx & 1) != me) {  // the other issuer's slot
+                    tr.next(a.nts);
+                    r.next(a.nd);
+                    continue;
+                  }
                   FM_TR(0, 1);
                   if (!(a.dbg & 512) && !((a.dbg & 256) && mbar_test_wait(bars.t_empty(tr.idx), tr.phase ^ 1u)) &&
                       !mbar_wait(bars.t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {

@@ -324,10 +324,10 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
     float qsm[32 * GQ];
 #pragma unroll
     for (int j = 0; j < 32 * GQ; ++j) qsm[j] = qsum_s[j];
-    // EW == 8: the two warps of a lane quarter take alternate documents, so the
-    // four warps of one set reduce a whole document (fewer lane reductions)
+    // EW == 8: the two warps of a lane quarter own alternate TMEM slots (the
+    // slot count is even), so every use of a slot is read by the same warp and
+    // no warp ever waits on a slot barrier more than one phase ahead
     const int half = (EW == 8) ? (warp - 2) / 4 : 0;
-    constexpr int EWD = EW == 8 ? 4 : EW;  // warps that score one document
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     const int tok_in_chunk = sub * 32 + lane;
     Ring ur, tr;
@@ -341,9 +341,8 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
       float rmax[32 * GQ];
 #pragma unroll
       for (int j = 0; j < 32 * GQ; ++j) rmax[j] = -INFINITY;
-      const bool mine = EW != 8 || (dloc & 1) == half;
       for (int c = 0; c < nch; ++c, ++kglob) {
-        if (!mine) {  // the other warp of this lane quarter takes the document
+        if (EW == 8 && (tr.idx & 1) != half) {  // the other warp of this lane quarter reads it
           tr.next(a.nts);
           ur.next(a.nu);
           continue;
@@ -394,7 +393,6 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         ur.next(a.nu);
       }
       if (!ok) break;
-      if (!mine) continue;
       float acc[GQ];
 #pragma unroll
       for (int g = 0; g < GQ; ++g) {
@@ -422,7 +420,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         if (!ok) break;
         __threadfence_block();
       }
-      const int ew = (warp - 2) % EWD;
+      const int ew = warp - 2;
 #pragma unroll
       for (int g = 0; g < GQ; ++g) xch[((slot * EW + ew) * GQ + g) * 32 + lane] = acc[g];
       __syncwarp();
@@ -432,13 +430,13 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         old = atomicAdd(&cnt[slot], 1);
       }
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == EWD - 1) {
+      if (old == EW - 1) {
         __threadfence_block();
         float tot = 0.f;
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
           float mm = -INFINITY;
-          for (int w = 0; w < EWD; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
+          for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
           tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
         }
         tot = warp_sum(tot);
