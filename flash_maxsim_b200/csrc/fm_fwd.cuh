@@ -632,9 +632,14 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
               } else {
                 // K split over several Q stages (single-document items only):
                 // every chunk slot of this M-block stays live until the last stage.
+                // (with two issuers each handles the chunks in its own slots)
                 {
                   Ring t = tr;
                   for (int c = 0; c < cn; ++c) {
+                    if (a.mma2 && (t.idx & 1) != me) {
+                      t.next(a.nts);
+                      continue;
+                    }
                     if (!mbar_wait(bars.t_empty(t.idx), t.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
                       ok = false;
                       break;
@@ -656,7 +661,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes) +
                                            ks * a.kq_atoms * b_atom;
                     const uint32_t tacc = tmem_base + t.idx * a.ts_stride;
-                    if (!skip_mma) {
+                    if (!skip_mma && !(a.mma2 && (t.idx & 1) != me)) {
 #pragma unroll
                       for (int kk = 0; kk < 8; ++kk) {
                         if (kk < ksteps) {
@@ -674,7 +679,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 }
                 if (!ok) break;
                 for (int c = 0; c < cn; ++c) {
-                  tc_commit(bars.t_full(tr.idx));
+                  if (!(a.mma2 && (tr.idx & 1) != me)) tc_commit(bars.t_full(tr.idx));
                   tr.next(a.nts);
                 }
               }
