@@ -153,6 +153,13 @@ bool plan_for_gd(const Shape& s, int gd, FwdArgs& a, int& smem_bytes) {
     a.C = std::min(a.C, cap);
     if (tune().C >= 16 && tune().C % 16 == 0 && tune().C <= std::min(256, cap)) a.C = tune().C;
   }
+  // two MMA issuers own alternate TMEM slots, so an odd slot count (3 slots of
+  // 160 columns) leaves them unbalanced: 192-token chunks give 2 slots at the
+  // same MMA cost (an M=128, K=16 MMA takes the same time for any N <= 192)
+  if (!int8 && tune().C == 0 && 512 / round_up(a.C, 32) == 3 && (a.nk == 1 || !s.argmax)) {
+    const int cap = ((kMaxSmem - 2 * a.kq_atoms * 16384 - 16 * 1024) / (a.d_atoms * 128)) / 16 * 16;
+    if (cap >= 192) a.C = 192;
+  }
   a.ts_stride = round_up(a.C, 32);
   a.nts = 512 / a.ts_stride;
   a.q_resident = (s.shared && a.R <= 4 && a.nk == 1) ? 1 : 0;
