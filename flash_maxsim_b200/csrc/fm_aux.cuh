@@ -256,56 +256,90 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
 // 256-element segment.  T = __half, float or __nv_bfloat16 (the reference
 // widens any input to fp32 before its min/max, so every type is quantised
 // from its own exact fp32 value).
-template <typename T>
+template <typename T, int LPR, int NR>
 __global__ void __launch_bounds__(256) quantize_int8_kernel(const T* __restrict__ D,
                                                             uint8_t* __restrict__ U,
                                                             __half* __restrict__ scales,
                                                             __half* __restrict__ mins, int64_t rows,
                                                             int d) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  // LPR lanes per row (8 elements each per segment), 32 / LPR rows per warp at
+  // a time and NR such row sets per warp, all loaded before any is converted
+  // (enough bytes in flight to stream HBM)
+  constexpr int RPW = 32 / LPR;
+  constexpr int SEG = NR > 1 ? 1 : kMaxSeg;  // several row sets only when a row fits one segment
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const T* src = D + row * d;
-  const int nseg = (d + 255) / 256;
-  float v[kMaxSeg][8];
-  float mn = INFINITY, mx = -INFINITY;
+  const int sub = lane / LPR, l = lane % LPR;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * RPW * NR + sub;
+  const int nseg = (d + LPR * 8 - 1) / (LPR * 8);
+  float v[NR][SEG][8];
+  float mn[NR], mx[NR];
 #pragma unroll
-  for (int s = 0; s < kMaxSeg; ++s) {
-    const int k = s * 256 + lane * 8;
-    if (s < nseg && k < d) {
-      load8(src + k, v[s]);
+  for (int r = 0; r < NR; ++r) {
+    const int64_t row = row0 + r * RPW;
+    mn[r] = INFINITY;
+    mx[r] = -INFINITY;
+    const T* src = D + (row < rows ? row : 0) * d;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        mn = fminf(mn, v[s][j]);
-        mx = fmaxf(mx, v[s][j]);
-      }
+    for (int s = 0; s < SEG; ++s) {
+      const int k = (s * LPR + l) * 8;
+      if (row < rows && s < nseg && k < d) load8(src + k, v[r][s]);
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  }
-  float scale = __fdiv_rn(__fsub_rn(mx, mn), 255.0f);
-  if (scale < 1e-8f) scale = 1e-8f;
-  uint8_t* dst = U + row * d;
+  for (int r = 0; r < NR; ++r) {
+    const bool live = row0 + r * RPW < rows;
 #pragma unroll
-  for (int s = 0; s < kMaxSeg; ++s) {
-    const int k = s * 256 + lane * 8;
-    if (s < nseg && k < d) {
-      uint32_t w[2] = {0u, 0u};
+    for (int s = 0; s < SEG; ++s) {
+      const int k = (s * LPR + l) * 8;
+      if (live && s < nseg && k < d) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float u = rintf(__fdiv_rn(__fsub_rn(v[s][j], mn), scale));
-        u = fminf(fmaxf(u, 0.f), 255.f);
-        w[j >> 2] |= static_cast<uint32_t>(u) << (8 * (j & 3));
+        for (int j = 0; j < 8; ++j) {
+          mn[r] = fminf(mn[r], v[r][s][j]);
+          mx[r] = fmaxf(mx[r], v[r][s][j]);
+        }
       }
-      *reinterpret_cast<uint2*>(dst + k) = make_uint2(w[0], w[1]);
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) {  // within the row's lanes
+      mn[r] = fminf(mn[r], __shfl_xor_sync(0xffffffffu, mn[r], o));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], o));
     }
   }
-  if (lane == 0) {
-    scales[row] = __float2half_rn(scale);
-    mins[row] = __float2half_rn(mn);
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const int64_t row = row0 + r * RPW;
+    if (row >= rows) continue;
+    float scale = __fdiv_rn(__fsub_rn(mx[r], mn[r]), 255.0f);
+    if (scale < 1e-8f) scale = 1e-8f;
+    uint8_t* dst = U + row * d;
+    // u = rint((x - min) / scale) with the IEEE quotient, as the reference
+    // does. The product with the rounded reciprocal is within 2 ulp (< 5e-5
+    // here, the quotient is <= 255) of the exact quotient, and rint only
+    // depends on which side of k + 0.5 the quotient lies: where the product is
+    // within 1e-4 of a half-integer the exact quotient is computed instead, so
+    // the codes equal the division's everywhere.
+    const float inv = __frcp_rn(scale);
+#pragma unroll
+    for (int s = 0; s < SEG; ++s) {
+      const int k = (s * LPR + l) * 8;
+      if (s < nseg && k < d) {
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float num = __fsub_rn(v[r][s][j], mn[r]);
+          float q = __fmul_rn(num, inv);
+          if (fabsf(__fsub_rn(__fsub_rn(q, floorf(q)), 0.5f)) < 1e-4f) q = __fdiv_rn(num, scale);
+          float u = rintf(q);
+          u = fminf(fmaxf(u, 0.f), 255.f);
+          w[j >> 2] |= static_cast<uint32_t>(u) << (8 * (j & 3));
+        }
+        *reinterpret_cast<uint2*>(dst + k) = make_uint2(w[0], w[1]);
+      }
+    }
+    if (l == 0) {
+      scales[row] = __float2half_rn(scale);
+      mins[row] = __float2half_rn(mn[r]);
+    }
   }
 }
 

@@ -786,22 +786,29 @@ int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, 
     return FM_ERR_ARG;
   if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_u8) & 7u)) return FM_ERR_ARG;
   if (rows == 0) return FM_OK;
-  const int64_t blocks = (rows + 7) / 8;
+  // lanes per row: 8 elements each, a power of two, up to a warp; rows that
+  // fit one segment are handled 4 row sets per warp
+  const int lpr = d <= 64 ? 8 : (d <= 128 ? 16 : 32);
+  const int nr = d <= 256 ? 4 : 1;
+  const int64_t rows_per_block = 8 * (32 / lpr) * nr;
+  const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (blocks > INT32_MAX) return FM_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned nb = static_cast<unsigned>(blocks);
   __half* sc = reinterpret_cast<__half*>(scales);
   __half* mn = reinterpret_cast<__half*>(mins);
+  auto launch = [&](auto tag) {
+    using T = decltype(tag);
+    const T* src = static_cast<const T*>(D);
+    if (lpr == 8) quantize_int8_kernel<T, 8, 4><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    else if (lpr == 16) quantize_int8_kernel<T, 16, 4><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    else if (nr == 4) quantize_int8_kernel<T, 32, 4><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    else quantize_int8_kernel<T, 32, 1><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+  };
   switch (dtype) {
-    case FM_DTYPE_F16:
-      quantize_int8_kernel<__half><<<nb, 256, 0, st>>>(static_cast<const __half*>(D), D_u8, sc, mn, rows, d);
-      break;
-    case FM_DTYPE_F32:
-      quantize_int8_kernel<float><<<nb, 256, 0, st>>>(static_cast<const float*>(D), D_u8, sc, mn, rows, d);
-      break;
-    case FM_DTYPE_BF16:
-      quantize_int8_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(D), D_u8, sc, mn, rows, d);
-      break;
+    case FM_DTYPE_F16: launch(__half{}); break;
+    case FM_DTYPE_F32: launch(float{}); break;
+    case FM_DTYPE_BF16: launch(__nv_bfloat16{}); break;
     default:
       return FM_ERR_ARG;
   }

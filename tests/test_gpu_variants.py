@@ -41,6 +41,28 @@ def test_quantize_bit_exact_vs_oracle(cuda, shape, dtype):
     np.testing.assert_array_equal(mn.cpu().numpy().view(np.uint16), omn.view(np.uint16))
 
 
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_quantize_bit_exact_many_rows_and_ties(cuda, dtype):
+    """Many rows plus rows whose exact quotients (x - min) / scale are
+    half-integers (rint ties to even): the kernel's codes must equal the IEEE
+    division's everywhere."""
+    import flash_maxsim_b200 as fm
+    (D,) = O.seeded_inputs(11, (2048, 128, 128), dtype=dtype)
+    ties = np.zeros((4, 128), dtype=np.float32)
+    ties[0] = np.arange(128) + 0.5           # min 0.5, max 127.5: scale 0.5
+    ties[0, 0], ties[0, 1] = 0.0, 255.0      # min 0, max 255: scale 1, quotients k + 0.5
+    ties[1] = 2 * np.arange(128) + 1.0       # scale 2 (max 510): odd values -> k + 0.5
+    ties[1, 0], ties[1, 1] = 0.0, 510.0
+    ties[2] = np.linspace(-3, 5, 128)
+    ties[3] = -ties[0]
+    D[0, :4] = ties.astype(dtype)
+    u8, sc, mn = fm.quantize_int8(dev(D, cuda))
+    ou, osc, omn = O.quantize_int8(D)
+    np.testing.assert_array_equal(u8.cpu().numpy(), ou)
+    np.testing.assert_array_equal(sc.cpu().numpy().view(np.uint16), osc.view(np.uint16))
+    np.testing.assert_array_equal(mn.cpu().numpy().view(np.uint16), omn.view(np.uint16))
+
+
 def test_quantize_bf16(cuda):
     import flash_maxsim_b200 as fm
     (D,) = O.seeded_inputs(3, (4, 50, 128), dtype=np.float32)
