@@ -374,6 +374,7 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   const int fixed = 1024 + round_up(q_bytes, 1024) + misc + (2 * a.nts + 2) * 8 + 32;
   a.nu = std::min(16, (kMaxSmem - fixed) / per_slot);
   if (tune().nd > 0) a.nu = std::min(a.nu, tune().nd);
+  a.nu &= ~1;  // even: paired epilogue warps and MMA issuers own alternate slots
   if (a.nu < 2) return false;
   uint32_t off = 0;
   a.off_q = off;

@@ -38,7 +38,8 @@ namespace fm {
 
 // two warps + 4 or 8 epilogue warps (8: two per TMEM lane quarter taking
 // alternate chunks, so every scheduler has two independent epilogue warps)
-__host__ __device__ constexpr int i8_threads(int epi_warps) { return (2 + epi_warps) * 32; }
+// (with 8 epilogue warps a second MMA issuer follows them: warp 10)
+__host__ __device__ constexpr int i8_threads(int epi_warps) { return (2 + epi_warps + (epi_warps == 8 ? 1 : 0)) * 32; }
 #ifndef FM_I8_TOKENS
 #define FM_I8_TOKENS 256
 #endif
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
       mbar_init(t_empty(i), 4);
     }
     mbar_init(q_ready, EW);
-    mbar_init(drain, 1);
+    mbar_init(drain, EW == 8 ? 2 : 1);  // every MMA issuer commits
     *abort_flag = 0;
     for (int i = 0; i < kI8Xch; ++i) {
       cnt[i] = 0;
@@ -215,9 +216,13 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         spin_drain(u_full(ur.idx), ur.phase, a);
       }
     }
-  } else if (warp == 1) {
-    // ===================== MMA issuer =====================
+  } else if (warp == 1 || (EW == 8 && warp == 2 + EW)) {
+    // ===================== MMA issuer(s) =====================
+    // With 8 epilogue warps two threads (warps 1 and 10) issue, each owning
+    // alternate TMEM slots; the slot counts (nts, nu) are even, so every use of
+    // a TMEM slot and of a staging slot is handled by the same issuer.
     if (lane == 0) {
+      const int me = warp == 1 ? 0 : 1;
       // A = uint8 chunk (unsigned, M = 128 tokens), B = split query (signed, N rows)
       const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) |
                              (static_cast<uint32_t>(a.N >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
@@ -231,6 +236,11 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         const int len = i8_len(a, b);
         const int nch = (len + kI8Tokens - 1) / kI8Tokens;
         for (int c = 0; c < nch; ++c) {
+          if (EW == 8 && (tr.idx & 1) != me) {  // the other issuer's slot
+            tr.next(a.nts);
+            ur.next(a.nu);
+            continue;
+          }
           // a half with no valid token is neither multiplied nor read by the epilogue
           const int nhalf = min(kI8Halves, (len - c * kI8Tokens + kI8Half - 1) / kI8Half);
           if (!mbar_wait(u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
@@ -258,7 +268,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
       tc_commit(drain);
       spin_drain(drain, 0, a);
     }
-  } else {
+  } else if (warp >= 2 && warp < 2 + EW) {
     // ===================== epilogue =====================
     const int sub = warp & 3;  // TMEM lane quarter = tokens [32 sub, 32 sub + 32) of a chunk
     const int et = threadIdx.x - 64;  // 0 .. 32 EW - 1
