@@ -505,7 +505,7 @@ def run_reference(args, cfg):
     if rank != 0:
         return
     desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
-    per_step = max(0.5, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    per_step = max(0.2, min(args.cpu_seconds, 120.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
         cpu_baseline(cfg, per_step / 2)
     vals = [cpu_baseline(cfg, per_step) for _ in range(args.steps)]
