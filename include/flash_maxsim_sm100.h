@@ -62,7 +62,10 @@ void fm_set_wait_timeout_ns(int64_t ns);
  * INT8 staging slots, Q stages per M-block, K atoms per Q stage, K atoms per
  * token, row groups per span, lane-quarter replication, Q resident flag, TMEM
  * slots, TMEM columns per slot, dynamic shared memory bytes, row groups per
- * document, documents per work item. No counterpart in the reference (its Triton autotuner picks tile
+ * document, documents per work item. The plan is that of the general forward
+ * kernel; one query of <= 64 rows with d <= 128 (dense or sparse) and the INT8
+ * shapes of fm_maxsim_int8_fwd's fast path run dedicated kernels instead.
+ * No counterpart in the reference (its Triton autotuner picks tile
  * sizes at run time, flash_maxsim/flash_maxsim.py:15-81).
  */
 int fm_fwd_plan_info(int mode, int argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
