@@ -46,6 +46,13 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
+// try_wait suspends the waiting thread until the phase completes or this many
+// nanoseconds pass (the bounded-wait loop re-checks its limit after each try):
+// waiting warps sleep instead of spinning, which measurably helps long runs
+// under the power cap. -DFM_NO_TRYWAIT_HINT builds the plain form.
+#if !defined(FM_TRYWAIT_HINT) && !defined(FM_NO_TRYWAIT_HINT)
+#define FM_TRYWAIT_HINT 1000000
+#endif
 #ifdef FM_TRYWAIT_HINT
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
