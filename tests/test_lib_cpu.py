@@ -67,6 +67,17 @@ def test_plans_fit_shared_memory(args):
         assert p["G"] <= p["nts"]
 
 
+def test_plan_even_tmem_slots_for_two_issuers():
+    """Config-2 shapes: 192-token chunks (2 TMEM slots, one per MMA issuer)
+    rather than 160 (3 slots); MMAs with N <= 192 cost the same."""
+    from flash_maxsim_b200._lib import plan_info
+    p = plan_info(0, False, 100, 100000, 32, 300, 128)
+    assert p["C"] == 192 and p["nts"] == 2
+    for args in [(0, False, 16, 4000, 1024, 1024, 128), (0, False, 8, 100, 32, 300, 128), (0, True, 3, 40, 64, 200, 128)]:
+        q = plan_info(*args)
+        assert q["nts"] >= 2 and q["ts_stride"] * q["nts"] <= 512
+
+
 def test_plan_groups_short_documents():
     from flash_maxsim_b200._lib import plan_info
     assert plan_info(0, False, 100, 100000, 32, 128, 128)["gd"] >= 2
