@@ -22,6 +22,7 @@ FM_ERR_BAD_INDEX = 20
 FM_ERR_UNSUPPORTED = 21
 FM_ERR_SCRATCH_TOO_SMALL = 23
 FM_DTYPE_F16 = 0
+FM_OPT_FLAT_KERNEL = 1
 FM_DTYPE_F32 = 1
 FM_DTYPE_BF16 = 2
 
@@ -33,6 +34,7 @@ SIGNATURES = {
     "fm_abi_version": (_I, []),
     "fm_status_string": (ctypes.c_char_p, [_I]),
     "fm_set_wait_timeout_ns": (None, [_I64]),
+    "fm_set_option": (_I, [_I, _I]),
     "fm_maxsim_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_int8_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_sparse_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
@@ -56,6 +58,12 @@ def plan_info(mode: int, argmax: bool, Nq: int, B: int, Lq: int, Ld: int, d: int
                               ctypes.cast(out, ctypes.c_void_p), len(PLAN_FIELDS))
     check(rc, "fm_fwd_plan_info")
     return dict(zip(PLAN_FIELDS, list(out)))
+
+
+def set_flat_kernel(enable: bool) -> None:
+    """Route eligible shared-document batches to the flat-token kernel
+    (process-wide; same scores, different tiling)."""
+    check(lib.fm_set_option(FM_OPT_FLAT_KERNEL, int(bool(enable))), "fm_set_option")
 
 
 def _load() -> ctypes.CDLL:
@@ -126,7 +134,62 @@ def status_word(device: torch.device) -> torch.Tensor:
 
 
 def sync_check_enabled() -> bool:
+    """FLASH_MAXSIM_SYNC_CHECK=1: synchronise and check after every call."""
     return os.environ.get("FLASH_MAXSIM_SYNC_CHECK", "0") not in ("", "0")
+
+
+class _Mirror:
+    """Pinned host copy of a device's status word, refreshed asynchronously
+    after every call; `event` marks when the copy has landed."""
+
+    def __init__(self, device: torch.device):
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = torch.cuda.Event()
+        self.pending = False
+
+
+_mirrors: dict[int, _Mirror] = {}
+
+
+def _raise_device_error(device: torch.device, code: int) -> None:
+    status_word(device).zero_()
+    raise RuntimeError(f"flash_maxsim_b200 device error: {status_string(code)} (code {code})")
+
+
+def poll_status(device: torch.device) -> None:
+    """Raise RuntimeError if an earlier call on `device` recorded a device-side
+    error whose asynchronous copy to the host has landed (no synchronisation)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    m = _mirrors.get(idx)
+    if m is None or not m.pending or not m.event.query():
+        return
+    m.pending = False
+    code = int(m.host[0])
+    if code != FM_OK:
+        m.host.zero_()
+        _raise_device_error(torch.device("cuda", idx), code)
+
+
+def after_call(device: torch.device) -> None:
+    """Make device-side errors visible without a synchronisation: the status
+    word is copied into pinned host memory behind the call on the current
+    stream, and the next call on this device (or check_status) raises when it
+    is non-zero. Under stream capture nothing is queued; with
+    FLASH_MAXSIM_SYNC_CHECK=1 every call synchronises and checks at once."""
+    if sync_check_enabled():
+        check_status(device)
+        return
+    if torch.cuda.is_current_stream_capturing():
+        return
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    m = _mirrors.get(idx)
+    if m is None:
+        m = _mirrors[idx] = _Mirror(torch.device("cuda", idx))
+    dev = torch.device("cuda", idx)
+    with on_device(dev):
+        m.host.copy_(status_word(dev), non_blocking=True)
+        m.event.record()
+    m.pending = True
 
 
 def check_status(device: torch.device | int | None = None) -> None:
@@ -142,7 +205,10 @@ def check_status(device: torch.device | int | None = None) -> None:
         device = torch.device("cuda", device)
     st = status_word(device)
     torch.cuda.synchronize(device)
+    m = _mirrors.get(device.index if device.index is not None else torch.cuda.current_device())
+    if m is not None:
+        m.pending = False
+        m.host.zero_()
     code = int(st.item())
     if code != FM_OK:
-        st.zero_()
-        raise RuntimeError(f"flash_maxsim_b200 device error: {status_string(code)} (code {code})")
+        _raise_device_error(device, code)

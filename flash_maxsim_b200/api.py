@@ -9,7 +9,8 @@ Error behaviour follows the reference: shape mismatches raise AssertionError
 (flash_maxsim/flash_maxsim.py:223,236,239,242; flash_maxsim_quant.py:22,113;
 flash_maxsim_sparse.py:115,119); a host-side launch error raises
 RuntimeError / ValueError; device-side errors land in the status word read by
-`check_status()`.
+`check_status()`, and (without a synchronisation) at the next call on the
+same device once an asynchronous copy of the status word has reached the host.
 """
 from __future__ import annotations
 
@@ -65,8 +66,12 @@ def _lengths(doc_lengths, n: int, Ld: int, device) -> torch.Tensor | None:
 
 
 def _after_call(device):
-    if _lib.sync_check_enabled():
-        _lib.check_status(device)
+    _lib.after_call(device)
+
+
+def _before_call(device):
+    # an error recorded by an earlier call on this device surfaces here
+    _lib.poll_status(device)
 
 
 def _fwd(Q3: torch.Tensor, D2: torch.Tensor, lengths, Nq, B, Lq, Ld, shared: bool,
@@ -78,6 +83,7 @@ def _fwd(Q3: torch.Tensor, D2: torch.Tensor, lengths, Nq, B, Lq, Ld, shared: boo
     if B == 0:
         return scores, argmax
     d = Q3.shape[-1]
+    _before_call(dev)
     with _lib.on_device(dev):
         rc = lib.fm_maxsim_fwd(
             Q3.data_ptr(), D2.data_ptr(), _lib.ptr(lengths), scores.data_ptr(),
@@ -181,6 +187,7 @@ class _FlashMaxSimFn(torch.autograd.Function):
         dev = Qh.device
         ws_bytes = int(lib.fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, dp))
         ws = torch.empty(max(ws_bytes, 0) // 4, device=dev, dtype=torch.float32) if ws_bytes > 0 else None
+        _before_call(dev)
         with _lib.on_device(dev):
             rc = lib.fm_maxsim_bwd(
                 Qh.data_ptr(), Dh.data_ptr(), argmax.data_ptr(), g.data_ptr(),
@@ -251,6 +258,7 @@ def quantize_int8(D: torch.Tensor):
     mins = torch.empty(B, Ld, 1, device=D.device, dtype=torch.float16)
     rows = B * Ld
     if rows:
+        _before_call(D.device)
         with _lib.on_device(D.device):
             rc = lib.fm_quantize_int8(x.data_ptr(), _QDTYPE[x.dtype], u8.data_ptr(),
                                       scales.data_ptr(), mins.data_ptr(), rows, dp,
@@ -296,6 +304,7 @@ def flash_maxsim_int8(Q: torch.Tensor, D_uint8: torch.Tensor, scales: torch.Tens
     if B == 0:
         return scores
     dev = Q.device
+    _before_call(dev)
     with _lib.on_device(dev):
         rc = lib.fm_maxsim_int8_fwd(Qh.data_ptr(), Du.data_ptr(), sc.data_ptr(), mn.data_ptr(),
                                     _lib.ptr(lengths), scores.data_ptr(), B, Lq, Ld,
@@ -338,6 +347,7 @@ def flash_maxsim_sparse(Q: torch.Tensor, D: torch.Tensor, indices: torch.Tensor,
     if B == 0:
         return scores
     dev = D.device
+    _before_call(dev)
     with _lib.on_device(dev):
         rc = lib.fm_maxsim_sparse_fwd(Qh.data_ptr(), Dh.data_ptr(), idx.data_ptr(),
                                       _lib.ptr(lengths), scores.data_ptr(), B, K, Lq, Ld,

@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dq_kernel(
       for (int u = 0; u < 4; ++u) {
         const int ti = __shfl_sync(0xffffffffu, t, (i + u) & 31);
         gi[u] = __shfl_sync(0xffffffffu, gv, (i + u) & 31);
-        const bool use = (i + u < nb) && ti >= 0;
+        const bool use = (i + u < nb) && ti >= 0 && ti < Ld;  // out-of-range entries count for nothing
         if (!use) gi[u] = 0.f;
         const __half* rowp = D + (static_cast<size_t>(b0 + i + u) * Ld + (use ? ti : 0)) * static_cast<size_t>(d);
 #pragma unroll

@@ -33,6 +33,7 @@ namespace {
 constexpr int kMaxSmem = 232448;        // 227 KB opt-in shared memory per CTA on sm_100
 constexpr int kMinSmem = 120 * 1024;    // keeps one CTA per SM (each owns all 512 TMEM columns)
 std::atomic<int64_t> g_timeout_ns{2000000000LL};
+std::atomic<int> g_flat_kernel{0};  // fm_set_option(FM_OPT_FLAT_KERNEL, 1)
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
 int cdiv(int x, int m) { return (x + m - 1) / m; }
@@ -78,11 +79,14 @@ bool make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* 
   return r == CUDA_SUCCESS;
 }
 
-// Optional plan overrides for tuning sweeps, e.g.
-// FLASH_MAXSIM_TUNE="nd=3,nq=3,gd=2" (read once per process).
+// Plan overrides for tuning sweeps, e.g. FLASH_MAXSIM_TUNE="nd=3,nq=3,gd=2",
+// read once per process.  Only tuning builds (-DFM_TUNING, never shipped) read
+// the variable: its `dbg` bits switch off MMAs, waits or whole kernels to
+// measure what is left, so a default build always uses the fixed plan below.
 struct Tune {
   int nd = 0, nq = 0, G = 0, C = 0, dbg = 0, gd = 0, flat = 0;
 };
+#ifdef FM_TUNING
 const Tune& tune() {
   static Tune t;
   static std::once_flag once;
@@ -107,6 +111,10 @@ const Tune& tune() {
   });
   return t;
 }
+#else
+constexpr Tune kNoTune{};
+constexpr const Tune& tune() { return kNoTune; }
+#endif
 
 struct Shape {
   int mode;
@@ -526,7 +534,7 @@ bool flat_ok(const Shape& s, const int32_t* lengths) {
   if (s.Lq % 32 != 0 || s.Nq * s.Lq < 128 || s.d > 128 || s.Lq / 32 > 4 * kFlatMaxJb) return false;
   // measured slower than the per-document kernel on B200 so far (the epilogue
   // cannot drain a 192-column chunk within one chunk's MMA time): opt-in only
-  if (s.Ld < 128 || !tune().flat) return false;
+  if (s.Ld < 128 || !(tune().flat || g_flat_kernel.load())) return false;
   return static_cast<int64_t>(s.B) * s.Ld + 2 * kFlatCT < (static_cast<int64_t>(1) << 31);
 }
 
@@ -624,12 +632,20 @@ const char* fm_status_string(int code) {
     case FM_ERR_UNSUPPORTED: return "shape not supported by the sm_100a kernels";
     case FM_ERR_NO_DEVICE: return "no CUDA device";
     case FM_ERR_SCRATCH_TOO_SMALL:
-      return "shape needs more dQ workspace than the 16 MiB built-in scratch of fm_maxsim_bwd_noalloc";
+      return "shape needs more dQ workspace than the 16 MiB built-in scratch of fm_maxsim_bwd_noalloc "
+             "(two document ranges of Nq * Lq * d fp32 partial sums must fit)";
   }
   return "unknown status";
 }
 
 void fm_set_wait_timeout_ns(int64_t ns) { g_timeout_ns.store(ns > 0 ? ns : 2000000000LL); }
+
+int fm_set_option(int option, int value) {
+  switch (option) {
+    case FM_OPT_FLAT_KERNEL: g_flat_kernel.store(value ? 1 : 0); return FM_OK;
+  }
+  return FM_ERR_ARG;
+}
 
 int fm_fwd_plan_info(int mode, int argmax, int Nq, int B, int Lq, int Ld, int d, int shared_docs,
                      int K, int32_t* out, int n_out) {
@@ -701,9 +717,15 @@ int64_t fm_maxsim_bwd_workspace_size(int Nq, int B, int Lq, int Ld, int d) {
   return ns > 1 ? static_cast<int64_t>(ns) * Nq * Lq * d * 4 : 0;
 }
 
-int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
-                  const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
-                  int Lq, int Ld, int d, void* workspace, int64_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace fm {
+namespace {
+// The backward with `ns` document ranges for dQ (ns > 1 needs a workspace of
+// ns * Nq * Lq * d fp32 values; ns == 1 writes dQ directly).
+int bwd_impl(const uint16_t* Q, const uint16_t* D, const int32_t* argmax, const float* grad_scores,
+             uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B, int Lq, int Ld, int d, int ns,
+             void* workspace, int64_t workspace_bytes, cudaStream_t st) {
   if (!Q || !D || !argmax || !grad_scores || !grad_Q || !grad_D) return FM_ERR_ARG;
   if (Nq < 1 || B < 0 || Lq < 1 || Ld < 1 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
   if (!aligned16(Q) || !aligned16(D) || !aligned16(grad_Q) || !aligned16(grad_D)) return FM_ERR_ARG;
@@ -711,14 +733,13 @@ int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
   if (E > 32768) return FM_ERR_UNSUPPORTED;
   const size_t smem = (static_cast<size_t>(Ld) + 1 + E) * 4 + static_cast<size_t>(Nq) * 4;
   if (smem > static_cast<size_t>(kMaxSmem)) return FM_ERR_UNSUPPORTED;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B == 0) {
     // no documents: dQ is zero
     return cudaMemsetAsync(grad_Q, 0, E * d * 2, st) == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
   }
-  const int64_t need = fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, d);
+  ns = std::max(1, std::min(ns, B));
+  const int64_t need = ns > 1 ? static_cast<int64_t>(ns) * E * d * 4 : 0;
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned16(workspace))) return FM_ERR_ARG;
-  const int ns = need > 0 ? dq_splits(Nq, B, Lq, Ld, d) : 1;
   const int per = cdiv(B, ns);
   dim3 gq(cdiv(static_cast<int>(E), 8), ns);
   const __half* Dh = reinterpret_cast<const __half*>(D);
@@ -755,30 +776,76 @@ int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+}  // namespace
+}  // namespace fm
+
+extern "C" {
+
+int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
+                  const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq, int B,
+                  int Lq, int Ld, int d, void* workspace, int64_t workspace_bytes, void* stream) {
+  const int ns = (Nq >= 1 && B >= 1 && Lq >= 1 && Ld >= 1 && d >= 8) ? dq_splits(Nq, B, Lq, Ld, d) : 1;
+  return bwd_impl(Q, D, argmax, grad_scores, grad_Q, grad_D, Nq, B, Lq, Ld, d, ns, workspace,
+                  workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int fm_maxsim_bwd_noalloc(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
                           const float* grad_scores, uint16_t* grad_Q, uint16_t* grad_D, int Nq,
                           int B, int Lq, int Ld, int d, void* stream) {
-  // the size limit is checked first, before any pointer is looked at
-  const int64_t need = fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, d);
-  if (need > static_cast<int64_t>(kNoAllocScratchBytes)) return FM_ERR_SCRATCH_TOO_SMALL;
+  if (Nq < 1 || B < 0 || Lq < 1 || Ld < 1 || d < 8) return FM_ERR_ARG;
+  // Fewer dQ document ranges than fm_maxsim_bwd would use when the usual count
+  // does not fit the scratch (ranges are still added in order, so the result
+  // is deterministic; with one range dQ is written directly, no scratch).
+  // The size limit is checked before any pointer is looked at.
+  // Shapes whose partial sums do not fit twice are refused: a single range
+  // would run every document through one CTA per row tile.
+  const int64_t per_range = static_cast<int64_t>(Nq) * Lq * d * 4;
+  int ns = B >= 1 ? dq_splits(Nq, B, Lq, Ld, d) : 1;
+  if (ns > 1 && static_cast<int64_t>(ns) * per_range > static_cast<int64_t>(kNoAllocScratchBytes)) {
+    if (2 * per_range > static_cast<int64_t>(kNoAllocScratchBytes)) return FM_ERR_SCRATCH_TOO_SMALL;
+    ns = static_cast<int>(static_cast<int64_t>(kNoAllocScratchBytes) / per_range);
+  }
   void* scratch = nullptr;
-  if (need > 0) {
+  if (ns > 1) {
     // Device address of the built-in scratch for the current device, looked up
-    // once per device (with that device current) and cached.
+    // with that device current and cached together with its CUDA context (a
+    // new context, e.g. after cudaDeviceReset, reloads the module and moves
+    // the array, so the address is looked up again).
     static std::mutex mu;
     static void* addr[64] = {nullptr};
+    static CUcontext ctx_of[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FM_ERR_NO_DEVICE;
+    auto get_ctx = ctx_get_current_fn();
+    if (!get_ctx) return FM_ERR_LAUNCH;
+    CUcontext ctx = nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (get_ctx(&ctx) != CUDA_SUCCESS) return FM_ERR_LAUNCH;
+    if (!addr[dev] || !ctx || ctx_of[dev] != ctx) {
+      // the lookup itself makes the device's primary context current if needed
       void* p = nullptr;
       if (cudaGetSymbolAddress(&p, g_fm_noalloc_scratch) != cudaSuccess || !p) return FM_ERR_LAUNCH;
+      if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return FM_ERR_LAUNCH;
       addr[dev] = p;
+      ctx_of[dev] = ctx;
     }
     scratch = addr[dev];
   }
-  return fm_maxsim_bwd(Q, D, argmax, grad_scores, grad_Q, grad_D, Nq, B, Lq, Ld, d, scratch,
-                       static_cast<int64_t>(kNoAllocScratchBytes), stream);
+  return bwd_impl(Q, D, argmax, grad_scores, grad_Q, grad_D, Nq, B, Lq, Ld, d, ns, scratch,
+                  static_cast<int64_t>(kNoAllocScratchBytes), static_cast<cudaStream_t>(stream));
 }
 
 int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,

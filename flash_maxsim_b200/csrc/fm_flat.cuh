@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1)
       const uint32_t idesc = idesc_f16_f32(128, kFlatCT);
       constexpr uint32_t d_atom = kFlatCT * 8u;  // one K atom of a document slot, 16-byte units
       const int ksteps = a.atoms * 4;
-      const bool skip_mma = (a.dbg & 2) != 0;
+      const bool skip_mma = FM_DBG(a, 2);
       Ring dr, qr, tr;
       bool ok = true;
       FM_TR_DECL;
@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     float* rows = reinterpret_cast<float*>(smem + a.off_rows);  // [2][kFlatDocSlots][128]
     float* xch = reinterpret_cast<float*>(smem + a.off_xch);    // [kFlatXch][4 quarters][kFlatSeg][32]
-    const bool skip_epi = (a.dbg & 1) != 0;
+    const bool skip_epi = FM_DBG(a, 1);
     Ring tr;
     uint32_t xph = 0u;
     int kc = 0;  // chunk counter (selects the exchange buffer)

@@ -45,11 +45,6 @@
 #include <cuda_fp16.h>
 #include "fm_ptx.cuh"
 
-#ifdef FM_EXP_NOFENCE
-#define FM_EXP_FENCE()
-#else
-#define FM_EXP_FENCE() tc_fence_after()
-#endif
 namespace fm {
 
 enum FwdMode : int { MODE_DENSE = 0, MODE_SPARSE = 1, MODE_INT8 = 2 };
@@ -93,7 +88,7 @@ struct FwdArgs {
   int q_resident;            // Q loaded once for the whole launch
   int q_flat;                // Lq % 32 == 0: an M-block is 128 consecutive rows of Q
   int mma2;                  // 1: two MMA issuers (warps 1 and 11) take alternate chunks
-  int dbg;                   // tuning experiments only: bit 0 skip epilogue reads, bit 1 skip MMAs
+  int dbg;  // tuning builds (FM_TUNING) only: bits that switch off parts of the work
   int nts;                   // TMEM accumulator slots
   int ts_stride;             // TMEM columns per slot
   int rowbuf;                // floats in the per-item row buffer
@@ -545,7 +540,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       const uint32_t idesc = idesc_f16_f32(128, a.C);
       const int ksteps = a.kq_atoms * 4;  // K=16 steps per Q stage (4 or 8)
       const uint32_t b_atom = a.C * 8u;    // one K atom of a D slot, in 16-byte units
-      const bool skip_mma = (a.dbg & 2) != 0;
+      const bool skip_mma = FM_DBG(a, 2);
       Ring dr, qr, tr;
       bool ok = true;
       FM_TR_DECL;
@@ -576,7 +571,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 const int qslot = a.q_resident ? 0 : qr.idx;
                 const uint32_t qph = a.q_resident ? 0u : qr.phase;
                 FM_TR(0, 5);
-                if (!((a.dbg & 1024) && qr.phase) && !((a.dbg & 256) && mbar_test_wait(bars.q_full(qslot), qph)) &&
+                if (!(FM_DBG(a, 1024) && qr.phase) && !(FM_DBG(a, 256) && mbar_test_wait(bars.q_full(qslot), qph)) &&
                     !mbar_wait(bars.q_full(qslot), qph, ctl, FM_ERR_TIMEOUT_QFULL)) {
                   ok = false;
                   break;
@@ -595,13 +590,13 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     continue;
                   }
                   FM_TR(0, 1);
-                  if (!(a.dbg & 512) && !((a.dbg & 256) && mbar_test_wait(bars.t_empty(tr.idx), tr.phase ^ 1u)) &&
+                  if (!FM_DBG(a, 512) && !(FM_DBG(a, 256) && mbar_test_wait(bars.t_empty(tr.idx), tr.phase ^ 1u)) &&
                       !mbar_wait(bars.t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
                     ok = false;
                     break;
                   }
                   FM_TR(0, 2);
-                  FM_EXP_FENCE();
+                  tc_fence_after();
                   const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes);
                   const uint32_t tacc = tmem_base + tr.idx * a.ts_stride;
                   FM_PROF_T0(pm0);
@@ -726,7 +721,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
     const int rep = a.rep;
     const int part = sub % rep;
     const int ppc = (a.C + 31) / 32;  // 32-column pieces per chunk
-    const bool skip_epi = (a.dbg & 1) != 0;
+    const bool skip_epi = FM_DBG(a, 1);
 
     float* qsum_s = reinterpret_cast<float*>(smem + a.off_qsum);
     if (MODE == MODE_INT8) {

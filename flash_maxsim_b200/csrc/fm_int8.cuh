@@ -64,7 +64,7 @@ struct Int8Args {
   size_t sc_total_bytes;   // bytes of the scales tensor (B * Ld * 2)
   uint32_t sc_slot_bytes;  // fp16 scale span + min span of one chunk
   uint32_t off_q, off_u, off_sc, off_misc, off_bar, u_slot_bytes;
-  int dbg;                 // tuning experiments only: bit 0 skip epilogue math, bit 1 skip MMAs
+  int dbg;  // tuning builds (FM_TUNING) only: bits that switch off parts of the work
 };
 
 __device__ __forceinline__ int i8_len(const Int8Args& a, int b) {
@@ -179,9 +179,9 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
           const size_t lo16 = byte0 & ~static_cast<size_t>(15);
           const uint32_t span =
               static_cast<uint32_t>((byte0 + kI8Tokens * 2 - lo16 + 15) & ~static_cast<size_t>(15));
-          const bool bulk_ok = lo16 + span <= a.sc_total_bytes && !(a.dbg & 4);
+          const bool bulk_ok = lo16 + span <= a.sc_total_bytes && !FM_DBG(a, 4);
           uint8_t* stage = smem + a.off_sc + ur.idx * a.sc_slot_bytes;
-          if (!bulk_ok && !(a.dbg & 4)) {
+          if (!bulk_ok && !FM_DBG(a, 4)) {
             // the span would run past the end of the tensors: plain loads (last chunk)
             __half* ss = reinterpret_cast<__half*>(stage);
             __half* ms = reinterpret_cast<__half*>(stage + a.sc_slot_bytes / 2);
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
           const uint32_t tacc = tmem_base + tr.idx * kI8Halves * a.N;
           for (int hb = 0; hb < nhalf; ++hb) {  // rows [128 hb, 128 hb + 128) of the chunk
             const uint64_t ah = au + hb * (kI8Half * 128u >> 4);
-            for (int at = 0; at < a.atoms && !(a.dbg & 2); ++at) {
+            for (int at = 0; at < a.atoms && !FM_DBG(a, 2); ++at) {
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per step, 4 steps per 128-byte atom
                 tc_mma_i8(tacc + hb * a.N, ah + at * u_atom + kk * 2u, bq + at * q_atom + kk * 2u,
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
             tmem_ld32(th + g * 32, reinterpret_cast<float(&)[32]>(h));
             tmem_ld32(th + 32 * GQ + g * 32, reinterpret_cast<float(&)[32]>(l));
             tmem_wait_ld();
-            if ((full || valid) && !(a.dbg & 1)) {
+            if ((full || valid) && !FM_DBG(a, 1)) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const int hl = static_cast<int>(h[j]) * 256 + static_cast<int>(l[j]);  // exact

@@ -100,6 +100,14 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   atomicCAS(status, 0, code);
 }
 
+#ifdef FM_TUNING
+// Tuning builds only (never shipped): the launch plan's `dbg` bits switch off
+// parts of the work (MMAs, epilogue reads, waits) to measure what is left.
+#define FM_DBG(a, bits) (((a).dbg & (bits)) != 0)
+#else
+#define FM_DBG(a, bits) false
+#endif
+
 #ifdef FM_PROFILE
 // Profiling builds only (never shipped): cycles spent in each kind of wait
 // (indexed by its timeout code) and in a few named sections, summed over the

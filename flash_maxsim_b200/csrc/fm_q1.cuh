@@ -53,7 +53,7 @@ struct Q1Args {
   const int32_t* sp_idx;    // sparse scoring: [B, K] query-row indices (negative ones wrap), else null
   int K;                   // indices per document (sparse scoring)
   int sparse;              // 1: score[b] = sum_k rowmax[idx[b, k]]
-  int dbg;                 // tuning experiments only: bit 0 skip epilogue math, bit 1 skip MMAs
+  int dbg;  // tuning builds (FM_TUNING) only: bits that switch off parts of the work
 };
 
 __device__ __forceinline__ int q1_len(const Q1Args& a, int b) {
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
           tc_fence_after();
           const uint64_t ad = smem_desc_sw128(sbase + a.off_u + ur.idx * a.u_slot_bytes);
           const uint32_t tacc = tmem_base + tr.idx * ts_stride;
-          if (!(a.dbg & 2)) {
+          if (!FM_DBG(a, 2)) {
 #pragma unroll
             for (int hb = 0; hb < NH; ++hb) {  // rows [128 hb, 128 hb + 128) of the chunk
               const uint64_t ah = ad + hb * (128u * 128u >> 4);
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
           tmem_ld32(th + g * 32, v0);
           if (NH == 2) tmem_ld32(th + a.N + g * 32, v1);
           tmem_wait_ld();
-          if (!(a.dbg & 1)) {
+          if (!FM_DBG(a, 1)) {
             if (full) {
 #pragma unroll
               for (int j = 0; j < 32; ++j)

@@ -56,6 +56,17 @@ const char* fm_status_string(int code);
 void fm_set_wait_timeout_ns(int64_t ns);
 
 /*
+ * Process-wide options (returns FM_ERR_ARG for an unknown option).
+ * FM_OPT_FLAT_KERNEL = 1 routes shared-document batches without doc_lengths
+ * (Ld >= 128, Lq % 32 == 0, d <= 128) to the flat-token kernel, which cuts
+ * the token matrix into fixed chunks across document boundaries (no MMA
+ * columns spent on chunk padding); 0 (default) keeps the per-document kernel.
+ * Both give the same scores. No counterpart in the reference.
+ */
+#define FM_OPT_FLAT_KERNEL 1
+int fm_set_option(int option, int value);
+
+/*
  * Launch plan the forward entry points would use for a shape (host only, no
  * device needed). mode: 0 dense, 1 sparse, 2 INT8. Writes 16 ints to `out`:
  * chunk tokens C, chunks per resident group G, D ring slots, Q ring stages,
@@ -139,10 +150,13 @@ int fm_maxsim_bwd(const uint16_t* Q, const uint16_t* D, const int32_t* argmax,
  * reserved by its own allocator, or that must not allocate once serving has
  * started. Nothing is allocated: the dQ partial sums go to a 16 MiB scratch
  * array compiled into the library (every device that loads the library keeps
- * it until the process exits). Shapes whose workspace
- * (fm_maxsim_bwd_workspace_size) exceeds 16 MiB are rejected with
- * FM_ERR_SCRATCH_TOO_SMALL. The first call on a device looks up the scratch
- * address for that device; make that first call before any stream capture.
+ * it until the process exits). When fm_maxsim_bwd's usual number of document
+ * ranges would need more than 16 MiB, fewer ranges are used (still added in a
+ * fixed order, so dQ may differ from fm_maxsim_bwd's in the last bits);
+ * shapes where two ranges of Nq * Lq * d fp32 partial sums exceed 16 MiB are
+ * rejected with FM_ERR_SCRATCH_TOO_SMALL. The first call on a device looks up
+ * the scratch address for that device (and again in a new CUDA context, e.g.
+ * after cudaDeviceReset); make that first call before any stream capture.
  * All calls share the one scratch array, so calls that overlap on the GPU
  * (different streams, or different host threads) race; serialise them. Every
  * partial sum is written before it is read, so nothing needs clearing between

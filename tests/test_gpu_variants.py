@@ -146,6 +146,24 @@ def test_sparse_bad_index_reported(cuda):
         fm.check_status(cuda)
 
 
+def test_device_error_raised_on_next_call_without_sync_check(cuda, monkeypatch):
+    # default behaviour: no synchronisation after the call, but the recorded
+    # error reaches the host asynchronously and the next call raises
+    import flash_maxsim_b200 as fm
+    monkeypatch.setenv("FLASH_MAXSIM_SYNC_CHECK", "0")
+    Q, D = O.seeded_inputs(5, (8, 128), (4, 16, 128))
+    idx = torch.tensor([[0, 1], [2, 99], [3, 4], [5, 6]], dtype=torch.int32, device=cuda)
+    fm.flash_maxsim_sparse(dev(Q, cuda), dev(D, cuda), idx)   # returns without raising
+    torch.cuda.synchronize(cuda)
+    with pytest.raises(RuntimeError, match="index"):
+        fm.flash_maxsim(dev(Q, cuda), dev(D, cuda))
+    # the word was cleared: the following calls are clean
+    fm.flash_maxsim(dev(Q, cuda), dev(D, cuda))
+    torch.cuda.synchronize(cuda)
+    fm.flash_maxsim(dev(Q, cuda), dev(D, cuda))
+    fm.check_status(cuda)
+
+
 # ---------------------------------------------------------------- training
 def _check_grads(Q, D, lens, g, dQ, dD, s):
     """Tie-aware gradient check: the GPU argmax must be an eps-argmax of the
