@@ -1,26 +1,35 @@
 """MaxSim scoring benchmark on B200 (one process per GPU; torchrun for N > 1).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--extra c1,c3,c4,c5]
+                    [--impl ours|reference]
 
-Default workload ("c2"): batched shared-docs scoring,
+Headline workload ("c2"): batched shared-docs scoring,
 Q [100, 32, 128] fp16 against D [100000, 300, 128] fp16 (7.68 GB), docs
 sharded across ranks (strong scaling: the 100000 docs are split N ways) and
 the per-rank score blocks combined with one NCCL all-gather. Inputs are
 synthetic: N(0, 1) entries, every token row L2-normalised, seeded per rank.
+At N = 1 the other BASELINE configurations (c1, c3, c4, c5) are measured in
+the same run and reported under "configs" of the same JSON line.
 
 A step = one pass of the hot path over the whole batch: the fused sm_100a
 MaxSim kernel on every rank, then the all-gather. Inputs (7.68 GB) exceed the
 126 MB L2, so no flush is needed between steps (configs whose documents are
 smaller than 4x L2 rotate over enough copies of them that no step finds its
-batch in L2). `value` is query-doc scores per second of the
+batch in L2). `value` is query-doc scores (or docs) per second of the
 whole job, device-timed with CUDA events, max over ranks. `e2e` repeats the
 step through the public API from pinned host buffers: host->device copy of Q
 and the rank's document shard, the kernel, the all-gather, and the
 device->host copy of the scores, all inside the timed region.
 
-`--impl reference` times the reference algorithm on the host CPU instead
-(the numpy restatement of the reference's maxsim_naive in oracle/, every host
-thread), on a bounded sample of the same workload per step; rank 0 only.
+After each timed region a seeded sample of documents of the timed output is
+checked against the CPU oracle (`parity`), and the reference's own Triton
+kernels (installed unmodified under baseline/_ref) are timed on the same
+inputs (`reference_gpu`).
+
+`--impl reference` times the reference's own CPU path instead (its torch
+maxsim_naive from baseline/_ref on every host thread; the numpy restatement
+in oracle/ when the reference is not installed), on a bounded sample of the
+same workload per step; rank 0 only.
 """
 from __future__ import annotations
 
@@ -197,63 +206,127 @@ def shard(B: int, rank: int, world: int):
 # our implementation
 # ---------------------------------------------------------------------------
 
-def run_ours(args, cfg):
+class Workload:
+    """Inputs of one configuration on this rank (documents of its shard)."""
+
+    def __init__(self, args, cfg, rank, world, dev):
+        import flash_maxsim_b200 as fm
+        desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
+        if args.docs:
+            # smaller document count, for ncu captures (same per-doc shapes)
+            B = args.docs
+            desc += f" [B overridden to {B}]"
+        for name in ("nq", "lq", "ld", "dim"):
+            v = getattr(args, "shape_" + name)
+            if v:
+                Nq, Lq, Ld, d = [v if n == name else o for n, o in zip(("nq", "lq", "ld", "dim"), (Nq, Lq, Ld, d))]
+                desc += f" [{name} overridden to {v}]"
+        self.cfg, self.desc, self.kind = cfg, desc, kind
+        self.Nq, self.Lq, self.B, self.Ld, self.d = Nq, Lq, B, Ld, d
+        lo, hi = shard(B, rank, world)
+        self.lo, self.Bl = lo, hi - lo
+        self.Q = synth((Nq, Lq, d) if kind not in ("single", "int8") else (Lq, d), 1, dev)
+        D = synth((self.Bl, Ld, d), 1000 + rank, dev)
+        self.lengths = None
+        if kind == "train":
+            gl = torch.Generator(device=dev).manual_seed(77 + rank)
+            self.lengths = torch.randint(32, Ld + 1, (self.Bl,), generator=gl, device=dev, dtype=torch.int32)
+        self.Du8 = self.sc = self.mn = None
+        if kind == "int8":
+            self.Du8, self.sc, self.mn = fm.quantize_int8(D)
+            del D
+            D = None
+            torch.cuda.empty_cache()
+        self.D = D
+        self.grad = None
+        if kind == "train":
+            self.grad = torch.randn(Nq, self.Bl, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+        self.in_bytes = ((self.Du8.numel() + self.sc.numel() * 2 + self.mn.numel() * 2) if kind == "int8"
+                         else D.numel() * 2)
+        # inputs smaller than 4x L2: rotate over enough copies of the documents
+        # that every step reads its batch from HBM (no step finds it in L2)
+        self.n_copies = 1
+        if self.in_bytes < 4 * L2_BYTES:
+            self.n_copies = -(-4 * L2_BYTES // self.in_bytes)
+        self.D_copies = [D] + [D.clone() for _ in range(self.n_copies - 1)] if D is not None else [None]
+        self.U_copies = ([(self.Du8, self.sc, self.mn)] +
+                         [(self.Du8.clone(), self.sc.clone(), self.mn.clone()) for _ in range(self.n_copies - 1)]
+                         if self.Du8 is not None else [None])
+
+    def call(self, i):
+        """One public-API scoring call on document copy i."""
+        import flash_maxsim_b200 as fm
+        if self.kind == "single":
+            return fm.flash_maxsim(self.Q, self.D_copies[i])
+        if self.kind == "batched":
+            return fm.flash_maxsim_batched(self.Q, self.D_copies[i])
+        u, s_, m_ = self.U_copies[i]
+        return fm.flash_maxsim_int8(self.Q, u, s_, m_)
+
+    def units(self):
+        return (self.Nq * self.B) if self.kind in ("batched", "train") else self.B
+
+    def unit_name(self):
+        return "query-doc scores/s" if self.kind in ("batched", "train") else "docs/s"
+
+
+def parity(w: Workload, out, dev) -> dict:
+    """Check a seeded sample of documents of the timed launch's output (copy 0
+    for rotated inputs) against the CPU oracle, after the timed region."""
+    from oracle import sampled_check as SC
+    import flash_maxsim_b200 as fm
+    npy = lambda t: t.detach().cpu().numpy()  # noqa: E731
+    t0 = time.perf_counter()
+    if w.kind in ("single", "batched"):
+        n = 24 if w.Lq * w.Ld > 100000 else 256
+        idx = SC.sample_docs(w.Bl, n, seed=11)
+        it = torch.from_numpy(idx).to(dev)
+        Q3 = w.Q if w.Q.dim() == 3 else w.Q.unsqueeze(0)
+        got = out if out.dim() == 2 else out.unsqueeze(0)
+        res = SC.check_scores(npy(Q3), npy(w.D_copies[0][it]), npy(got[:, it]))
+    elif w.kind == "int8":
+        idx = SC.sample_docs(w.Bl, 256, seed=11)
+        it = torch.from_numpy(idx).to(dev)
+        res = SC.check_int8(npy(w.Q), npy(w.Du8[it]), npy(w.sc[it]), npy(w.mn[it]), npy(out[it]))
+    else:
+        from flash_maxsim_b200 import api
+        Qg = w.Q.detach().clone().requires_grad_(True)
+        Dg = w.D.detach().clone().requires_grad_(True)
+        s = fm.flash_maxsim_train(Qg, Dg, w.lengths)
+        s.backward(w.grad)
+        _, am = api._fwd(w.Q, w.D, w.lengths, w.Nq, w.Bl, w.Lq, w.Ld, True, True)
+        am = am.view(w.Nq, w.Bl, w.Lq)
+        idx = SC.sample_docs(w.Bl, 16, seed=11)
+        it = torch.from_numpy(idx).to(dev)
+        rows = [(0, 0), (w.Nq // 2, w.Lq - 1), (w.Nq - 1, w.Lq // 3)]
+        Dsel = []
+        ar = torch.arange(w.Bl, device=dev)
+        for n, q in rows:
+            a = am[n, :, q].long()
+            sel = w.D[ar, a.clamp(min=0)].float()
+            Dsel.append(npy(torch.where((a >= 0)[:, None], sel, torch.zeros_like(sel))))
+        sd = s.detach()
+        g_eff = torch.where(torch.isfinite(sd), w.grad, torch.zeros_like(w.grad))
+        res = SC.check_train(npy(w.Q), npy(w.D[it]), npy(w.lengths[it]), npy(w.grad[:, it]), npy(sd[:, it]),
+                             npy(am[:, it]), npy(Dg.grad[it].float()), rows,
+                             np.stack([npy(Qg.grad[n, q].float()) for n, q in rows]), (npy(g_eff), Dsel))
+        res = {k: v for k, v in res.items() if k != "parts"} | {
+            "parts": {k: v["ok"] for k, v in res["parts"].items()}}
+    res["docs_sampled"] = int(len(idx))
+    res["seconds"] = round(time.perf_counter() - t0, 1)
+    res["oracle"] = "oracle/maxsim_oracle.py (numpy restatement of maxsim_naive, pinned to reference golden vectors)"
+    return res
+
+
+def run_config(args, cfg, rank, world, dev, headline: bool) -> dict:
     import flash_maxsim_b200 as fm
     from flash_maxsim_b200 import sharded
 
-    desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
-    if args.docs:
-        # smaller document count, for ncu captures (same per-doc shapes)
-        B = args.docs
-        desc += f" [B overridden to {B}]"
-    for name in ("nq", "lq", "ld", "dim"):
-        v = getattr(args, "shape_" + name)
-        if v:
-            Nq, Lq, Ld, d = [v if n == name else o for n, o in zip(("nq", "lq", "ld", "dim"), (Nq, Lq, Ld, d))]
-            desc += f" [{name} overridden to {v}]"
-    rank, world, dev = dist_setup(args.gpus)
-    lo, hi = shard(B, rank, world)
-    Bl = hi - lo
     peaks = load_peaks()
     torch.manual_seed(0)
-
-    Q = synth((Nq, Lq, d) if kind != "single" and kind != "int8" else (Lq, d), 1, dev)
-    D = synth((Bl, Ld, d), 1000 + rank, dev)
-    lengths = None
-    if kind == "train":
-        gl = torch.Generator(device=dev).manual_seed(77 + rank)
-        lengths = torch.randint(32, Ld + 1, (Bl,), generator=gl, device=dev, dtype=torch.int32)
-    Du8 = sc = mn = None
-    if kind == "int8":
-        Du8, sc, mn = fm.quantize_int8(D)
-        del D
-        D = None
-        torch.cuda.empty_cache()
-    grad = None
-    if kind == "train":
-        grad = torch.randn(Nq, Bl, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
-
-    in_bytes = (Du8.numel() + sc.numel() * 2 + mn.numel() * 2) if kind == "int8" else D.numel() * 2
-    # inputs smaller than 4x L2: rotate over enough copies of the documents that
-    # every step reads its batch from HBM (no step finds its documents in L2)
-    n_copies = 1
-    if in_bytes < 4 * L2_BYTES:
-        n_copies = -(-4 * L2_BYTES // in_bytes)
-    D_copies = [D] + [D.clone() for _ in range(n_copies - 1)] if D is not None else [None]
-    U_copies = ([(Du8, sc, mn)] + [(Du8.clone(), sc.clone(), mn.clone()) for _ in range(n_copies - 1)]
-                if Du8 is not None else [None])
-    step_idx = [0]
-
+    w = Workload(args, cfg, rank, world, dev)
+    kind, Nq, Lq, B, Ld, d, Bl = w.kind, w.Nq, w.Lq, w.B, w.Ld, w.d, w.Bl
     stream = torch.cuda.current_stream(dev)
-
-    def call(i):
-        """One public-API call on document copy i."""
-        if kind == "single":
-            return fm.flash_maxsim(Q, D_copies[i])
-        if kind == "batched":
-            return fm.flash_maxsim_batched(Q, D_copies[i])
-        u, s_, m_ = U_copies[i]
-        return fm.flash_maxsim_int8(Q, u, s_, m_)
 
     # Scoring calls are captured once per document copy in a CUDA graph and
     # replayed, so short launches are not limited by Python dispatch; the
@@ -263,24 +336,25 @@ def run_ours(args, cfg):
         side = torch.cuda.Stream(dev)
         side.wait_stream(stream)
         with torch.cuda.stream(side):
-            for i in range(n_copies):
-                call(i)
+            for i in range(w.n_copies):
+                w.call(i)
         stream.wait_stream(side)
         torch.cuda.synchronize(dev)
-        for i in range(n_copies):
+        for i in range(w.n_copies):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                graph_out.append(call(i))
+                graph_out.append(w.call(i))
             graphs.append(g)
         torch.cuda.synchronize(dev)
     only_kernel = world == 1 and kind != "train"
     ev_pool = [torch.cuda.Event(enable_timing=True) for _ in range(2 * (args.steps + args.warmup))]
+    step_idx = [0]
 
     def kernel_step():
         """The hot path once; returns (result, kernel start/end events)."""
         k = step_idx[0]
         step_idx[0] += 1
-        i = k % n_copies
+        i = k % w.n_copies
         e0, e1 = ev_pool[(2 * k) % len(ev_pool)], ev_pool[(2 * k + 1) % len(ev_pool)]
         if only_kernel:
             # the step is this one launch: the timed region's own events time it
@@ -291,12 +365,12 @@ def run_ours(args, cfg):
             graphs[i].replay()
             out = graph_out[i]
         elif kind != "train":
-            out = call(i)
+            out = w.call(i)
         else:
-            Qg = Q.detach().requires_grad_(True)
-            Dg = D.detach().requires_grad_(True)
-            s = fm.flash_maxsim_train(Qg, Dg, lengths)
-            s.backward(grad)
+            Qg = w.Q.detach().requires_grad_(True)
+            Dg = w.D.detach().requires_grad_(True)
+            s = fm.flash_maxsim_train(Qg, Dg, w.lengths)
+            s.backward(w.grad)
             out = s.detach()
         if e1 is not None:
             e1.record(stream)
@@ -336,17 +410,14 @@ def run_ours(args, cfg):
         kern_ms = [a.elapsed_time(b) for a, b in evs]
         kern_avg_ms = max_over_ranks(sum(kern_ms) / len(kern_ms), world, dev)
 
-    units_total = (Nq * B) if kind in ("batched", "train") else B
-    unit_name = "query-doc scores/s" if kind in ("batched", "train") else "docs/s"
-    value = units_total / (total_ms / 1e3 / args.steps)
+    value = w.units() / (total_ms / 1e3 / args.steps)
 
     # roofline of the dominant kernel (per rank, per launch)
-    units_rank = (Nq * Bl) if kind in ("batched", "train") else Bl
     flops = 2.0 * Nq * Lq * Ld * d * Bl
     if kind == "train":
-        flops = 2.0 * Nq * Lq * float(lengths.sum().item()) * d
+        flops = 2.0 * Nq * Lq * float(w.lengths.sum().item()) * d
     if kind in ("single", "int8"):
-        alg_bytes = in_bytes + Q.numel() * 2 + Bl * 4
+        alg_bytes = w.in_bytes + w.Q.numel() * 2 + Bl * 4
         achieved = alg_bytes / (kern_avg_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
@@ -360,56 +431,65 @@ def run_ours(args, cfg):
                 # the same against cuBLAS held for seconds under the 1 kW power cap
                 "frac_of_sustained_peak": (round(achieved / peaks["tflops_sustained"], 4)
                                            if peaks.get("tflops_sustained") else None),
-                "hbm_achieved_GBs": round(in_bytes / (kern_avg_ms / 1e3) / 1e9, 1)}
+                "hbm_achieved_GBs": round(w.in_bytes / (kern_avg_ms / 1e3) / 1e9, 1)}
+        if kind == "train":
+            roof["note"] = ("step = forward with argmax + backward (dQ, dD); flops of the forward on "
+                            "valid tokens over the whole step's time")
     tr = load_traffic(cfg)
     roof["traffic"] = tr.get("bytes_per_launch") if tr else None
     if tr:
         roof["traffic_source"] = tr.get("source")
     roof["kernel_ms"] = round(kern_avg_ms, 4)
 
+    out_for_check = graph_out[0] if graphs else None
+    if out_for_check is None and kind != "train":
+        out_for_check = w.call(0)
+    par = None
+    if rank == 0 and not args.no_parity:
+        par = parity(w, out_for_check, dev)
+
     # end to end through the public API from pinned host memory
-    e2e = None if args.no_e2e else run_e2e(args, kind, fm, sharded, Q, D, Du8, sc, mn, lengths, grad,
-                                           B, Bl, world, dev, units_total, unit_name)
+    e2e = None if args.no_e2e else run_e2e(args, w, fm, sharded, world, dev)
+
+    ref_gpu = None
+    if rank == 0 and world == 1 and not args.no_ref_gpu:
+        ref_gpu = reference_gpu(args, w, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cfg, args.cpu_seconds)
+        cpu = cpu_baseline(cfg, args.cpu_seconds if headline else min(args.cpu_seconds, 4.0))
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 1), "unit": unit_name, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "strong",
-            "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
-            "data": "synthetic N(0,1), rows L2-normalised, seeded",
-            "config": {"workload": desc, "config": cfg, "Nq": Nq, "Lq": Lq, "B": B, "Ld": Ld, "d": d,
-                       "docs_per_rank": Bl, "parallelism": f"doc-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                       "launch": "CUDA graph replay of the public API call" if graphs else "eager public API call",
-                       "l2": "inputs larger than L2" if n_copies == 1 else
-                       f"documents rotated over {n_copies} copies ({n_copies * in_bytes / 1e6:.0f} MB > 4x L2) between steps"},
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * (3 if kind == "train" else 1),
-            "clocks": clocks,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    res = {
+        "value": round(value, 1), "unit": w.unit_name(), "ms_per_step": round(total_ms / args.steps, 4),
+        "config": {"workload": w.desc, "config": cfg, "Nq": Nq, "Lq": Lq, "B": B, "Ld": Ld, "d": d,
+                   "docs_per_rank": Bl,
+                   "parallelism": f"doc-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "launch": "CUDA graph replay of the public API call" if graphs else "eager public API call",
+                   "l2": "inputs larger than L2" if w.n_copies == 1 else
+                   f"documents rotated over {w.n_copies} copies ({w.n_copies * w.in_bytes / 1e6:.0f} MB > 4x L2) "
+                   "between steps"},
+        "roofline": roof, "kernel_ms": round(kern_avg_ms, 4), "clocks": clocks, "parity": par,
+        "e2e": e2e, "cpu_baseline": cpu, "reference_gpu": ref_gpu,
+        "gpu_launches": args.steps * (3 if kind == "train" else 1),
+    }
+    del w, graphs, graph_out, out_for_check
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return res
 
 
-def run_e2e(args, kind, fm, sharded, Q, D, Du8, sc, mn, lengths, grad, B, Bl, world, dev,
-            units_total, unit_name):
+def run_e2e(args, w: Workload, fm, sharded, world, dev):
     """Same step through the public API, inputs from pinned host buffers."""
+    kind = w.kind
     steps = max(2, min(args.steps, args.e2e_steps))
-    hQ = Q.cpu().pin_memory()
+    hQ = w.Q.cpu().pin_memory()
     if kind == "int8":
-        hD = [Du8.cpu().pin_memory(), sc.cpu().pin_memory(), mn.cpu().pin_memory()]
-        dD = [torch.empty_like(Du8), torch.empty_like(sc), torch.empty_like(mn)]
+        hD = [w.Du8.cpu().pin_memory(), w.sc.cpu().pin_memory(), w.mn.cpu().pin_memory()]
+        dD = [torch.empty_like(w.Du8), torch.empty_like(w.sc), torch.empty_like(w.mn)]
     else:
-        hD = [D.cpu().pin_memory()]
-        dD = [torch.empty_like(D)]
-    hL = lengths.cpu().pin_memory() if lengths is not None else None
+        hD = [w.D.cpu().pin_memory()]
+        dD = [torch.empty_like(w.D)]
+    hL = w.lengths.cpu().pin_memory() if w.lengths is not None else None
     h2d = hQ.numel() * hQ.element_size() + sum(t.numel() * t.element_size() for t in hD)
     if hL is not None:
         h2d += hL.numel() * 4
@@ -432,11 +512,11 @@ def run_e2e(args, kind, fm, sharded, Q, D, Du8, sc, mn, lengths, grad, B, Bl, wo
             qg = q.requires_grad_(True)
             dg = dD[0].requires_grad_(True)
             s = fm.flash_maxsim_train(qg, dg, ln)
-            s.backward(grad)
+            s.backward(w.grad)
             out = s.detach()
             dD[0] = dg.detach()
         if world > 1:
-            out = sharded.all_gather_scores(out if out.dim() == 2 else out.unsqueeze(0), B)
+            out = sharded.all_gather_scores(out if out.dim() == 2 else out.unsqueeze(0), w.B)
         if out_host is None:
             out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
             d2h = out.numel() * out.element_size()
@@ -454,50 +534,155 @@ def run_e2e(args, kind, fm, sharded, Q, D, Du8, sc, mn, lengths, grad, B, Bl, wo
     b.record(stream)
     torch.cuda.synchronize(dev)
     ms = max_over_ranks(a.elapsed_time(b), world, dev) / steps
-    return {"value": round(units_total / (ms / 1e3), 1), "unit": unit_name,
+    return {"value": round(w.units() / (ms / 1e3), 1), "unit": w.unit_name(),
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
             "ms_per_step": round(ms, 3)}
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (the reference algorithm on the host cores)
+# the reference implementation (installed unmodified under baseline/_ref)
 # ---------------------------------------------------------------------------
 
-def _cpu_sample_inputs(cfg: str, n_docs: int):
-    from oracle import maxsim_oracle as O
-    desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
-    nq = 1 if kind in ("single", "int8") else min(Nq, 4)
-    Q, D = O.seeded_inputs(123, (nq, Lq, d), (n_docs, Ld, d))
-    return O, Q, D, nq, kind
+def reference_module():
+    """The reference package from baseline/_ref, or None when it is absent or
+    does not import."""
+    p = ROOT / "baseline" / "_ref"
+    if not (p / "flash_maxsim").exists():
+        return None
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+    try:
+        import flash_maxsim
+        return flash_maxsim
+    except Exception:  # noqa: BLE001 (any import failure means "not available")
+        return None
+
+
+def reference_gpu(args, w: Workload, dev):
+    """The reference's own Triton kernels on this GPU, same inputs, for
+    comparison (median of a few launches after its autotuning)."""
+    ref = reference_module()
+    if ref is None:
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    if w.kind == "train":
+        return {"unavailable": "the reference's training path takes one query and no doc_lengths "
+                               "(flash_maxsim/flash_maxsim.py:253-291)"}
+    try:
+        D = w.D_copies[0]
+        if w.kind == "single":
+            fn = lambda: ref.flash_maxsim(w.Q, D)  # noqa: E731
+        elif w.kind == "batched":
+            fn = lambda: ref.flash_maxsim_batched(w.Q, D)  # noqa: E731
+        else:
+            fn = lambda: ref.flash_maxsim_int8(w.Q, w.Du8, w.sc, w.mn)  # noqa: E731
+        fn()
+        fn()  # autotuning happens on the first calls
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(3):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            out = fn()
+            b.record()
+            torch.cuda.synchronize(dev)
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        ours = graph_out_first(w)
+        same = None
+        if ours is not None:
+            o = out if out.dim() == ours.dim() else out.view_as(ours)
+            same = float((o.float() - ours.float()).abs().max().item())
+        return {"value": round(w.units() / (ms / 1e3), 1), "unit": w.unit_name(), "ms_per_step": round(ms, 4),
+                "impl": "reference Triton kernels (baseline/_ref, unmodified)",
+                "max_abs_diff_vs_ours": same}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+
+
+def graph_out_first(w: Workload):
+    try:
+        with torch.no_grad():
+            return w.call(0)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference's own CPU path, maxsim_naive, on the host cores)
+# ---------------------------------------------------------------------------
+
+def _cpu_sample_docs(kind, Lq, Ld, d) -> int:
+    # a sample whose one pass is well under a second on a many-core host
+    work = Lq * Ld * d
+    return max(8, min(256, int(2.5e9 // work)))
 
 
 def cpu_baseline(cfg: str, seconds: float):
-    """Reference maxsim (numpy port of maxsim_naive) on a bounded sample of the
-    workload, with every host thread; returns units per second."""
+    """The reference's maxsim_naive (torch, fp32, baseline/_ref) on a bounded
+    sample of the workload with every host thread, or, if the reference does
+    not import, the numpy restatement in oracle/; returns units per second.
+    Training samples run the forward and the autograd backward."""
+    from oracle import maxsim_oracle as O
     desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
-    n_docs = 256
-    O, Q, D, nq, kind = _cpu_sample_inputs(cfg, n_docs)
+    n_docs = _cpu_sample_docs(kind, Lq, Ld, d)
+    nq = 1 if kind in ("single", "int8") else min(Nq, 4)
+    Q, D = O.seeded_inputs(123, (nq, Lq, d), (n_docs, Ld, d))
+    lens = None
+    if kind == "train":
+        lens = np.random.default_rng(5).integers(32, Ld + 1, n_docs).astype(np.int32)
     if kind == "int8":
         u8, s, m = O.quantize_int8(D)
         D = O.dequantize_int8(u8, s, m)
-    # every host thread, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1)
-    from threadpoolctl import threadpool_limits
     threads = os.cpu_count() or 1
-    with threadpool_limits(limits=threads):
+    ref = reference_module()
+    old_threads = torch.get_num_threads()
+    if ref is not None:
+        torch.set_num_threads(threads)
+        Qt = torch.from_numpy(np.asarray(Q, dtype=np.float32))
+        Dt = torch.from_numpy(np.asarray(D, dtype=np.float32))
+        Lt = torch.from_numpy(lens) if lens is not None else None
+        g = torch.randn(n_docs, generator=torch.Generator().manual_seed(1))
+
+        def one_pass():
+            for n in range(nq):
+                if kind == "train":
+                    q = Qt[n].clone().requires_grad_(True)
+                    dd = Dt.clone().requires_grad_(True)
+                    s = ref.maxsim_naive(q, dd, Lt)
+                    (s * g).sum().backward()
+                else:
+                    ref.maxsim_naive(Qt[n], Dt)
+        what = ("the reference's maxsim_naive (torch fp32 einsum, baseline/_ref)"
+                + (" forward + autograd backward" if kind == "train" else ""))
+        used = torch.get_num_threads()
+        kind_s = "reference"
+    else:
+        from threadpoolctl import threadpool_limits
+
+        def one_pass():
+            with threadpool_limits(limits=threads):
+                for n in range(nq):
+                    O.maxsim(Q[n], D, lens)
+        what = "numpy fp32 restatement of maxsim_naive (oracle/maxsim_oracle.py; reference not installed)"
+        used = threads
+        kind_s = "port"
+    try:
         t0 = time.perf_counter()
         done = 0
         while True:
-            for n in range(nq):
-                O.maxsim(Q[n], D)
+            one_pass()
             done += 1
             el = time.perf_counter() - t0
             if el >= seconds:
                 break
+    finally:
+        torch.set_num_threads(old_threads)
     units = done * n_docs * (nq if kind in ("batched", "train") else 1)
     unit_name = "query-doc scores/s" if kind in ("batched", "train") else "docs/s"
-    return {"value": round(units / el, 1), "unit": unit_name, "cores": int(threads), "kind": "port",
-            "sample": f"{nq} queries x {n_docs} docs of the {cfg} shapes, repeated for {el:.1f} s "
-                      "(numpy fp32 restatement of maxsim_naive, oracle/maxsim_oracle.py)"}
+    return {"value": round(units / el, 1), "unit": unit_name, "cores": int(used), "kind": kind_s,
+            "torch_threads": int(used) if ref is not None else None, "os_cpu_count": os.cpu_count(),
+            "sample": f"{nq} queries x {n_docs} docs of the {cfg} shapes, repeated for {el:.1f} s ({what})"}
 
 
 def run_reference(args, cfg):
@@ -517,11 +702,38 @@ def run_reference(args, cfg):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), rows L2-normalised, seeded",
         "ms_per_step": round(per_step * 1e3, 1),
         "config": {"workload": desc, "config": cfg, "Nq": Nq, "Lq": Lq, "B": B, "Ld": Ld, "d": d},
-        "cpu_baseline": {"value": v, "unit": base["unit"], "cores": base["cores"], "kind": "port",
-                         "sample": base["sample"]},
+        "cpu_baseline": {k: base[k] for k in ("unit", "cores", "kind", "sample", "torch_threads", "os_cpu_count")}
+        | {"value": v},
         "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    rank, world, dev = dist_setup(args.gpus)
+    head = run_config(args, args.config, rank, world, dev, headline=True)
+    extras = {}
+    if world == 1 and args.extra:
+        for c in [c.strip() for c in args.extra.split(",") if c.strip()]:
+            if c != args.config:
+                extras[c] = run_config(args, c, rank, world, dev, headline=False)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic N(0,1), rows L2-normalised, seeded",
+            "config": head["config"], "roofline": head["roofline"], "cpu_baseline": head["cpu_baseline"],
+            "e2e": head["e2e"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+            "parity": head["parity"], "reference_gpu": head["reference_gpu"],
+        }
+        if extras:
+            line["configs"] = extras
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 def main():
@@ -529,12 +741,16 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS), help="headline configuration")
+    ap.add_argument("--extra", default="c1,c3,c4,c5",
+                    help="further configurations measured in the same run at N=1 (empty: none)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's Triton kernels")
     ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly (no CUDA graph)")
     for name in ("nq", "lq", "ld", "dim"):
         ap.add_argument(f"--shape-{name}", type=int, default=0, help="override a shape (tuning)")
@@ -545,7 +761,7 @@ def main():
     if args.impl == "reference":
         run_reference(args, args.config)
     else:
-        run_ours(args, args.config)
+        run_ours(args)
 
 
 if __name__ == "__main__":

@@ -161,7 +161,9 @@ def poll_status(device: torch.device) -> None:
     error whose asynchronous copy to the host has landed (no synchronisation)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     m = _mirrors.get(idx)
-    if m is None or not m.pending or not m.event.query():
+    if m is None or not m.pending or torch.cuda.is_current_stream_capturing():
+        return
+    if not m.event.query():
         return
     m.pending = False
     code = int(m.host[0])
