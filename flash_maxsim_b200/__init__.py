@@ -10,6 +10,9 @@ from ._lib import check_status, LOADED_PATH  # noqa: F401  (loads the CUDA libra
 from .api import (  # noqa: F401
     flash_maxsim,
     flash_maxsim_batched,
+    flash_maxsim_topk,
+    flash_maxsim_batched_topk,
+    topk_scores,
     flash_maxsim_train,
     maxsim_naive,
     flash_maxsim_int8,
@@ -22,6 +25,9 @@ from .api import (  # noqa: F401
 __all__ = [
     "flash_maxsim",
     "flash_maxsim_batched",
+    "flash_maxsim_topk",
+    "flash_maxsim_batched_topk",
+    "topk_scores",
     "flash_maxsim_train",
     "maxsim_naive",
     "flash_maxsim_int8",

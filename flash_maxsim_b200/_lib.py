@@ -44,6 +44,10 @@ SIGNATURES = {
     "fm_quantize_int8": (_I, [_P, _I, _P, _P, _P, _I64, _I, _P]),
     "fm_wait_selftest": (_I, [_P, _I64, _P]),
     "fm_fwd_plan_info": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I]),
+    "fm_topk_workspace_size": (_I64, [_I, _I]),
+    "fm_maxsim_topk": (_I, [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _P, _I64, _P, _P]),
+    "fm_topk_select": (_I, [_P, _I, _I, _I, _I64, _P, _P, _P, _I64, _P]),
+    "fm_topk_merge": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
 }
 
 PLAN_FIELDS = ("C", "G", "nd", "nq", "nu", "nk", "kq_atoms", "d_atoms", "RS", "rep",

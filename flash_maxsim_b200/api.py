@@ -154,6 +154,113 @@ def flash_maxsim_batched(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None,
 
 
 # ---------------------------------------------------------------------------
+# top-k (callers of the reference: examples/demo.py:126-134, benchmarks/bench.py:36)
+# ---------------------------------------------------------------------------
+
+def _topk_workspace(Nq: int, k: int, device) -> torch.Tensor:
+    nbytes = int(lib.fm_topk_workspace_size(Nq, k))
+    if nbytes <= 0:
+        raise ValueError(f"top-k workspace unavailable for Nq={Nq}, k={k} (1 <= k <= 1024)")
+    return torch.empty(-(-nbytes // 16) * 4, dtype=torch.float32, device=device)
+
+
+def flash_maxsim_batched_topk(Q: torch.Tensor, D: torch.Tensor, k: int, doc_lengths=None):
+    """The k best shared documents of every query: Q [Nq, Lq, d], D [B, Ld, d]
+    -> (values fp32 [Nq, k], document ids int64 [Nq, k]).
+
+    Same scores as flash_maxsim_batched; the scoring kernel keeps each query's
+    k best documents per CTA and one merge kernel combines them, so the
+    [Nq, B] matrix is never sorted. Order: score descending, ties by the lower
+    document id. 1 <= k <= min(B, 1024)."""
+    assert Q.dim() == 3 and D.dim() == 3 and Q.shape[2] == D.shape[2]
+    _require_cuda(Q, D)
+    Nq, Lq, d = Q.shape
+    B, Ld, _ = D.shape
+    k = int(k)
+    assert 1 <= k <= B, f"k={k} outside [1, {B}]"
+    lengths = _lengths(doc_lengths, B, Ld, D.device)
+    dev = D.device
+    if Nq == 0:
+        return (torch.empty(0, k, device=dev, dtype=torch.float32),
+                torch.empty(0, k, device=dev, dtype=torch.int64))
+    if Lq == 0 or Ld == 0:
+        return topk_scores(_degenerate(Nq, B, Lq, Ld, dev), k)
+    Qh, Dh = _half(Q), _half(D)
+    scores = torch.empty(Nq, B, device=dev, dtype=torch.float32)
+    vals = torch.empty(Nq, k, device=dev, dtype=torch.float32)
+    idx = torch.empty(Nq, k, device=dev, dtype=torch.int64)
+    ws = _topk_workspace(Nq, k, dev)
+    _before_call(dev)
+    with _lib.on_device(dev):
+        rc = lib.fm_maxsim_topk(Qh.data_ptr(), Dh.data_ptr(), _lib.ptr(lengths), scores.data_ptr(), k,
+                                vals.data_ptr(), idx.data_ptr(), Nq, B, Lq, Ld, Qh.shape[-1],
+                                ws.data_ptr(), ws.numel() * 4, _lib.status_word(dev).data_ptr(),
+                                _lib.stream_of(dev))
+    _lib.check(rc, "fm_maxsim_topk")
+    _after_call(dev)
+    return vals, idx
+
+
+def flash_maxsim_topk(Q: torch.Tensor, D: torch.Tensor, k: int, doc_lengths=None):
+    """The k best documents for one query: Q [Lq, d], D [B, Ld, d] ->
+    (values fp32 [k], document ids int64 [k]); see flash_maxsim_batched_topk."""
+    assert Q.dim() == 2
+    v, i = flash_maxsim_batched_topk(Q.unsqueeze(0), D, k, doc_lengths)
+    return v.squeeze(0), i.squeeze(0)
+
+
+def topk_scores(scores: torch.Tensor, k: int, id_offset: int = 0):
+    """GPU top-k of any score matrix [Nq, B] (or vector [B]), e.g. from
+    flash_maxsim_int8 or flash_maxsim_sparse: (values, ids + id_offset),
+    score descending, ties by the lower id."""
+    _require_cuda(scores)
+    vec = scores.dim() == 1
+    s2 = scores.unsqueeze(0) if vec else scores
+    assert s2.dim() == 2
+    Nq, B = s2.shape
+    k = int(k)
+    assert 1 <= k <= B, f"k={k} outside [1, {B}]"
+    s2 = s2.float().contiguous()
+    dev = s2.device
+    vals = torch.empty(Nq, k, device=dev, dtype=torch.float32)
+    idx = torch.empty(Nq, k, device=dev, dtype=torch.int64)
+    if Nq:
+        ws = _topk_workspace(Nq, k, dev)
+        with _lib.on_device(dev):
+            rc = lib.fm_topk_select(s2.data_ptr(), Nq, B, k, int(id_offset), vals.data_ptr(), idx.data_ptr(),
+                                    ws.data_ptr(), ws.numel() * 4, _lib.stream_of(dev))
+        _lib.check(rc, "fm_topk_select")
+    return (vals.squeeze(0), idx.squeeze(0)) if vec else (vals, idx)
+
+
+def topk_merge_candidates(values: torch.Tensor, ids: torch.Tensor, k: int):
+    """Merge per-part candidate lists values/ids [Nq, parts, k'] (ids < 0 =
+    none; ids below 2**31) into the k best per query, on the GPU."""
+    _require_cuda(values, ids)
+    assert values.dim() == 3 and values.shape == ids.shape
+    Nq, parts, kk = values.shape
+    k = int(k)
+    assert 1 <= k <= 1024
+    v = values.float()
+    i = ids.to(torch.int32)
+    if kk < k:  # pad each part's list to k entries
+        v = F.pad(v, (0, k - kk), value=float("-inf"))
+        i = F.pad(i, (0, k - kk), value=-1)
+    elif kk > k:
+        v, i = v[..., :k], i[..., :k]  # lists are sorted: the first k suffice
+    v, i = v.contiguous(), i.contiguous()
+    dev = v.device
+    vals = torch.empty(Nq, k, device=dev, dtype=torch.float32)
+    idx = torch.empty(Nq, k, device=dev, dtype=torch.int64)
+    if Nq:
+        with _lib.on_device(dev):
+            rc = lib.fm_topk_merge(v.data_ptr(), i.data_ptr(), Nq, parts, k, vals.data_ptr(), idx.data_ptr(),
+                                   _lib.stream_of(dev))
+        _lib.check(rc, "fm_topk_merge")
+    return vals, idx
+
+
+# ---------------------------------------------------------------------------
 # training (flash_maxsim/flash_maxsim.py:253-291)
 # ---------------------------------------------------------------------------
 

@@ -18,6 +18,7 @@
 #include "fm_int8.cuh"
 #include "fm_q1.cuh"
 #include "fm_flat.cuh"
+#include "fm_topk.cuh"
 
 // Scratch for fm_maxsim_bwd_noalloc: the dQ partial sums live here instead of
 // in caller-provided memory.  Every device that loads this library keeps
@@ -290,6 +291,7 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tq2, const CUtensorMap&
   if (sms <= 0) return FM_ERR_NO_DEVICE;
   const int grid = std::max(1, std::min(a.n_work, sms));
   const int threads = MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16;
+  if (a.topk.k > 0 && a.topk.parts != grid) return FM_ERR_ARG;  // set by fwd_common
   kern<<<grid, threads, smem, stream>>>(tq, tq2, td, a);
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
@@ -299,11 +301,14 @@ bool flat_ok(const Shape& s, const int32_t* lengths);
 int launch_flat(const Shape& s, const void* Q, const void* D, float* scores, int32_t* status,
                 cudaStream_t stream);
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
-              const int32_t* sp_idx, int32_t* status, cudaStream_t stream);
+              const int32_t* sp_idx, int32_t* status, cudaStream_t stream, TopkArgs* topk);
 
+// Forward launch for any shape.  `topk` (optional): when the chosen kernel
+// selects per-CTA top-k candidates in its tail (one query or shared dense
+// documents), topk->parts is set to its grid; otherwise it stays 0.
 int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
                int32_t* argmax, const int32_t* sp_idx, const void* scales, const void* mins,
-               int32_t* status, cudaStream_t stream) {
+               int32_t* status, cudaStream_t stream, TopkArgs* topk = nullptr) {
   if (!Q || !D || !scores || !status) return FM_ERR_ARG;
   if (s.Nq < 1 || s.B < 0 || s.Lq < 1 || s.Ld < 1 || s.d < 8 || s.d > 2048) return FM_ERR_ARG;
   if (s.d % 8 != 0) return FM_ERR_ARG;
@@ -315,8 +320,9 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   const int64_t n_docs = s.shared ? s.B : static_cast<int64_t>(s.Nq) * s.B;
   if (n_docs > INT32_MAX || static_cast<int64_t>(s.Nq) * s.B > INT32_MAX) return FM_ERR_ARG;
 
-  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, sp_idx, status, stream);
-  if (flat_ok(s, lengths)) return launch_flat(s, Q, D, scores, status, stream);
+  if (topk) topk->parts = 0;
+  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, sp_idx, status, stream, topk);
+  if (!topk && flat_ok(s, lengths)) return launch_flat(s, Q, D, scores, status, stream);
 
   FwdArgs a{};
   int smem = 0;
@@ -330,6 +336,13 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   a.mins = static_cast<const __half*>(mins);
   a.status = status;
   a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
+  a.topk = TopkArgs{0, 0, nullptr, nullptr};
+  if (topk && topk->k > 0 && s.mode == MODE_DENSE && !s.argmax && s.shared) {
+    const int sms = sm_count();
+    if (sms <= 0) return FM_ERR_NO_DEVICE;
+    topk->parts = std::max(1, std::min(a.n_work, sms));
+    a.topk = *topk;
+  }
 
   CUtensorMap tq, tq2, td;
   const int nq_rows = s.mode == MODE_DENSE ? s.Nq : 1;
@@ -502,7 +515,7 @@ int launch_q1_t(const CUtensorMap& tq, const CUtensorMap& td, const Q1Args& a, i
 }
 
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
-              const int32_t* sp_idx, int32_t* status, cudaStream_t stream) {
+              const int32_t* sp_idx, int32_t* status, cudaStream_t stream, TopkArgs* topk) {
   const int CT = tune().C == 256 ? 256 : 128;
   Q1Args a{};
   int smem = 0;
@@ -515,6 +528,13 @@ int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengt
   a.sparse = s.mode == MODE_SPARSE ? 1 : 0;
   a.sp_idx = sp_idx;
   a.K = s.mode == MODE_SPARSE ? s.K : 0;
+  a.topk = TopkArgs{0, 0, nullptr, nullptr};
+  if (topk && topk->k > 0) {
+    const int sms = sm_count();
+    if (sms <= 0) return FM_ERR_NO_DEVICE;
+    topk->parts = std::max(1, std::min(a.B, sms));  // the grid of launch_q1_t
+    a.topk = *topk;
+  }
   CUtensorMap tq, td;
   if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, 1, 64, a.N,
                    CU_TENSOR_MAP_SWIZZLE_128B))
@@ -697,6 +717,50 @@ int fm_maxsim_sparse_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* in
 
 namespace fm {
 namespace {
+bool topk_smem_ready() {
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    const int bytes = (kTopkThreads / 32 + 1) * kTopkMaxK * 8;
+    ok = cudaFuncSetAttribute(topk_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+             cudaSuccess &&
+         cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+             cudaSuccess;
+  });
+  return ok;
+}
+
+// Candidate workspace: Nq x parts x k (score, id) pairs, parts <= SM count.
+int64_t topk_ws_bytes(int Nq, int k) {
+  const int sms = sm_count();
+  if (sms <= 0) return -1;
+  return static_cast<int64_t>(Nq) * sms * k * 8;
+}
+
+// Stage 1 over a score matrix (parts = min(B, SMs)) unless `parts_done`
+// candidates already exist, then stage 2.
+int topk_finish(const float* scores, int Nq, int B, int k, TopkArgs t, int parts_done, float* top_s,
+                int64_t* top_i, int64_t id_offset, cudaStream_t st) {
+  if (!topk_smem_ready()) return FM_ERR_LAUNCH;
+  const int W = kTopkThreads / 32;
+  if (parts_done == 0) {
+    const int sms = sm_count();
+    if (sms <= 0) return FM_ERR_NO_DEVICE;
+    t.parts = std::max(1, std::min(B, sms));
+    topk_partial_kernel<<<dim3(Nq, t.parts), kTopkThreads, W * k * 8, st>>>(scores, B, t);
+    if (cudaGetLastError() != cudaSuccess) return FM_ERR_LAUNCH;
+  } else {
+    t.parts = parts_done;
+  }
+  topk_merge_kernel<<<Nq, kTopkThreads, (W + 1) * k * 8, st>>>(t, top_s, top_i, id_offset);
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+bool topk_ws_ok(int Nq, int k, const void* ws, int64_t ws_bytes) {
+  const int64_t need = topk_ws_bytes(Nq, k);
+  return need > 0 && ws && ws_bytes >= need && aligned16(ws);
+}
+
 // Document ranges of the dQ pass: enough CTAs to fill the GPU (>= 2 per SM),
 // ranges whose documents fit comfortably in L2 (<= 64 MB), >= 8 docs each.
 int dq_splits(int Nq, int B, int Lq, int Ld, int d) {
@@ -710,6 +774,44 @@ int dq_splits(int Nq, int B, int Lq, int Ld, int d) {
 }  // namespace fm
 
 extern "C" {
+
+int64_t fm_topk_workspace_size(int Nq, int k) {
+  if (Nq < 1 || k < 1 || k > kTopkMaxK) return 0;
+  const int64_t b = topk_ws_bytes(Nq, k);
+  return b > 0 ? b : 0;
+}
+
+int fm_maxsim_topk(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengths, float* scores, int k,
+                   float* top_scores, int64_t* top_idx, int Nq, int B, int Lq, int Ld, int d,
+                   void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
+  if (!top_scores || !top_idx || k < 1 || k > kTopkMaxK || B < 1 || k > B || Nq < 1) return FM_ERR_ARG;
+  if (!topk_ws_ok(Nq, k, workspace, workspace_bytes)) return FM_ERR_ARG;
+  const int64_t cand = static_cast<int64_t>(Nq) * sm_count() * k;
+  TopkArgs t{k, 0, static_cast<float*>(workspace), reinterpret_cast<int32_t*>(static_cast<float*>(workspace) + cand)};
+  Shape s{MODE_DENSE, false, Nq, B, Lq, Ld, d, 0, 1};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rc = fwd_common(s, Q, D, doc_lengths, scores, nullptr, nullptr, nullptr, nullptr, status, st, &t);
+  if (rc != FM_OK) return rc;
+  return topk_finish(scores, Nq, B, k, t, t.parts, top_scores, top_idx, 0, st);
+}
+
+int fm_topk_select(const float* scores, int Nq, int B, int k, int64_t id_offset, float* top_scores,
+                   int64_t* top_idx, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!scores || !top_scores || !top_idx || Nq < 1 || B < 1 || k < 1 || k > kTopkMaxK || k > B)
+    return FM_ERR_ARG;
+  if (!topk_ws_ok(Nq, k, workspace, workspace_bytes)) return FM_ERR_ARG;
+  const int64_t cand = static_cast<int64_t>(Nq) * sm_count() * k;
+  TopkArgs t{k, 0, static_cast<float*>(workspace), reinterpret_cast<int32_t*>(static_cast<float*>(workspace) + cand)};
+  return topk_finish(scores, Nq, B, k, t, 0, top_scores, top_idx, id_offset, static_cast<cudaStream_t>(stream));
+}
+
+int fm_topk_merge(const float* cand_scores, const int32_t* cand_ids, int Nq, int parts, int k,
+                  float* top_scores, int64_t* top_idx, void* stream) {
+  if (!cand_scores || !cand_ids || !top_scores || !top_idx || Nq < 1 || parts < 1 || k < 1 || k > kTopkMaxK)
+    return FM_ERR_ARG;
+  TopkArgs t{k, parts, const_cast<float*>(cand_scores), const_cast<int32_t*>(cand_ids)};
+  return topk_finish(nullptr, Nq, 0, k, t, parts, top_scores, top_idx, 0, static_cast<cudaStream_t>(stream));
+}
 
 int64_t fm_maxsim_bwd_workspace_size(int Nq, int B, int Lq, int Ld, int d) {
   if (Nq < 1 || B < 1 || Lq < 1 || Ld < 1 || d < 8) return 0;

@@ -44,6 +44,7 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 #include "fm_ptx.cuh"
+#include "fm_topk.cuh"
 
 namespace fm {
 
@@ -94,6 +95,7 @@ struct FwdArgs {
   int rowbuf;                // floats in the per-item row buffer
   uint32_t off_q, off_d, off_u, off_sc, off_state, off_rows, off_xch, off_qsum, off_bar;
   uint32_t q_stage_bytes, d_slot_bytes, u_slot_bytes;
+  TopkArgs topk;             // k > 0 (dense shared docs): per-CTA top-k candidates in the tail
 };
 
 // Position in a ring of n slots: slot index and the parity of the current lap.
@@ -1055,6 +1057,25 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
+  }
+  if (MODE == MODE_DENSE && !ARGMAX && a.topk.k > 0 && a.shared && !*abort_flag) {
+    // Top-k tail: every warp takes queries in turn and selects the k best of the
+    // documents this CTA scored (work items w0, w0 + wstep, ...; gd documents
+    // each), read back from the score matrix this CTA just wrote (L2-resident;
+    // plain loads, the data is not read-only during the kernel).
+    const int nwarps = blockDim.x >> 5;
+    const int count = ((a.n_work - w0 + wstep - 1) / wstep) * a.gd;
+    for (int n = warp; n < a.Nq; n += nwarps) {
+      const float* row = a.scores + static_cast<size_t>(n) * a.B;
+      const size_t o = (static_cast<size_t>(n) * a.topk.parts + blockIdx.x) * a.topk.k;
+      warp_topk<24>(count, a.topk.k,
+                    [&](int p) {
+                      const int j = p / a.gd;
+                      const int b = (w0 + j * wstep) * a.gd + (p - j * a.gd);
+                      return b < a.B ? TopkCand{row[b], b} : TopkCand{0.f, -1};
+                    },
+                    a.topk.cand_s + o, a.topk.cand_b + o, lane);
+    }
   }
 }
 

@@ -54,6 +54,7 @@ struct Q1Args {
   int K;                   // indices per document (sparse scoring)
   int sparse;              // 1: score[b] = sum_k rowmax[idx[b, k]]
   int dbg;  // tuning builds (FM_TUNING) only: bits that switch off parts of the work
+  TopkArgs topk;           // k > 0: per-CTA top-k candidates in the tail
 };
 
 __device__ __forceinline__ int q1_len(const Q1Args& a, int b) {
@@ -377,6 +378,18 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
+  }
+  if (a.topk.k > 0 && warp == 2 && !*abort_flag) {
+    // Top-k tail: the k best of the documents this CTA scored (w0, w0 + wstep,
+    // ...), read back from the scores it just wrote (plain loads).
+    const int count = (a.B - w0 + wstep - 1) / wstep;
+    const size_t o = static_cast<size_t>(blockIdx.x) * a.topk.k;
+    warp_topk<8>(count, a.topk.k,
+                 [&](int p) {
+                   const int b = w0 + p * wstep;
+                   return TopkCand{a.scores[b], b};
+                 },
+                 a.topk.cand_s + o, a.topk.cand_b + o, lane);
   }
 }
 

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from .api import flash_maxsim_batched
+from .api import flash_maxsim_batched, flash_maxsim_batched_topk, topk_merge_candidates
 
 
 def shard_range(B: int, rank: int, world: int) -> tuple[int, int]:
@@ -61,6 +61,7 @@ def topk_merge(local: torch.Tensor, k: int, B: int, group=None):
     Each rank keeps its own top-min(k, B_rank), the candidates (score, global
     doc id) of all ranks are all-gathered, and the merge takes the top-k of
     the world * k candidates. Ties are broken towards the lower document id.
+    CUDA scores are selected and merged by the library's top-k kernels.
     Returns (values [Nq, k], doc ids int64 [Nq, k]) on every rank.
     """
     world, rank = _world(group)
@@ -71,6 +72,20 @@ def topk_merge(local: torch.Tensor, k: int, B: int, group=None):
         raise ValueError(f"k={k} outside [1, {B}]")
     Nq = local.shape[0]
     kk = min(k, local.shape[1])
+    if local.is_cuda:
+        # per-rank selection and the final merge run as GPU kernels
+        from .api import topk_merge_candidates, topk_scores
+        vals = torch.full((Nq, k), float("-inf"), dtype=torch.float32, device=local.device)
+        ids = torch.full((Nq, k), -1, dtype=torch.int32, device=local.device)
+        if kk > 0:
+            v, i = topk_scores(local, kk, id_offset=lo)
+            vals[:, :kk] = v
+            ids[:, :kk] = i.to(torch.int32)
+        cand_v = torch.stack(_gather_padded(vals, group), dim=1)  # [Nq, world, k]
+        cand_i = torch.stack(_gather_padded(ids, group), dim=1)
+        return topk_merge_candidates(cand_v, cand_i, k)
+    # CPU-resident scores (host-side logic, e.g. gloo ranks): the same order
+    # with torch sorts
     vals = torch.full((Nq, k), float("-inf"), dtype=torch.float32, device=local.device)
     ids = torch.full((Nq, k), torch.iinfo(torch.int64).max, dtype=torch.int64, device=local.device)
     if kk > 0:
@@ -102,7 +117,23 @@ def sharded_maxsim_batched(Q: torch.Tensor, D_local: torch.Tensor, B: int, doc_l
     """Score a doc-sharded corpus: this rank holds documents shard_range(B, ...)
     as D_local [B_rank, Ld, d]. Returns the gathered [Nq, B] scores, or the
     merged (values, doc ids) top-k when `topk` is given."""
-    local = flash_maxsim_batched(Q, D_local, doc_lengths_local)
     if topk is not None:
-        return topk_merge(local, topk, B, group)
+        world, rank = _world(group)
+        lo, hi = shard_range(B, rank, world)
+        Nq = Q.shape[0]
+        k = int(topk)
+        if not (1 <= k <= B):
+            raise ValueError(f"k={k} outside [1, {B}]")
+        vals = torch.full((Nq, k), float("-inf"), dtype=torch.float32, device=Q.device)
+        ids = torch.full((Nq, k), -1, dtype=torch.int32, device=Q.device)
+        kk = min(k, hi - lo)
+        if kk > 0:
+            # the scoring kernel keeps this rank's top-k itself
+            v, i = flash_maxsim_batched_topk(Q, D_local, kk, doc_lengths_local)
+            vals[:, :kk] = v
+            ids[:, :kk] = (i + lo).to(torch.int32)
+        cand_v = torch.stack(_gather_padded(vals, group), dim=1)
+        cand_i = torch.stack(_gather_padded(ids, group), dim=1)
+        return topk_merge_candidates(cand_v, cand_i, k)
+    local = flash_maxsim_batched(Q, D_local, doc_lengths_local)
     return all_gather_scores(local, B, group)

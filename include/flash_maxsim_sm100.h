@@ -125,6 +125,35 @@ int fm_maxsim_sparse_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* in
                          int Ld, int d, int32_t* status, void* stream);
 
 /*
+ * Top-k documents per query (score descending, then document id ascending;
+ * deterministic). Rerankers keep only these (the reference's callers run
+ * `scores.topk(k)` on the full matrix: examples/demo.py:126-134,
+ * benchmarks/bench.py:36; the reference library has no top-k entry point).
+ *
+ * fm_topk_workspace_size: bytes of the candidate workspace for Nq queries
+ *   and k (depends on the current device's SM count); 16-byte aligned.
+ * fm_maxsim_topk: fm_maxsim_fwd (shared documents) whose kernel also keeps
+ *   each query's k best documents per CTA, then one merge kernel. scores
+ *   [Nq, B] is still written in full; top_scores fp32 [Nq, k], top_idx
+ *   int64 [Nq, k]. 1 <= k <= min(B, 1024).
+ * fm_topk_select: the same selection over any score matrix [Nq, B] (e.g. of
+ *   fm_maxsim_int8_fwd); id_offset is added to every document id (the first
+ *   document of a shard).
+ * fm_topk_merge: final merge of candidates cand_scores / cand_ids
+ *   [Nq, parts, k] (ids < 0 = none), e.g. the per-rank top-k lists of a
+ *   document-sharded corpus after an all-gather.
+ * No counterpart in the reference.
+ */
+int64_t fm_topk_workspace_size(int Nq, int k);
+int fm_maxsim_topk(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengths, float* scores, int k,
+                   float* top_scores, int64_t* top_idx, int Nq, int B, int Lq, int Ld, int d,
+                   void* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+int fm_topk_select(const float* scores, int Nq, int B, int k, int64_t id_offset, float* top_scores,
+                   int64_t* top_idx, void* workspace, int64_t workspace_bytes, void* stream);
+int fm_topk_merge(const float* cand_scores, const int32_t* cand_ids, int Nq, int parts, int k,
+                  float* top_scores, int64_t* top_idx, void* stream);
+
+/*
  * Training backward from the forward's argmax (shared docs).
  *   grad_Q[n,q,:] = sum_b g[n,b] * D[b, argmax[n,b,q], :]
  *   grad_D[b,t,:] = sum_{(n,q): argmax[n,b,q]==t} g[n,b] * Q[n,q,:]
