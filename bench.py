@@ -448,6 +448,11 @@ def run_config(args, cfg, rank, world, dev, headline: bool) -> dict:
     if rank == 0 and not args.no_parity:
         par = parity(w, out_for_check, dev)
 
+    # the same scoring with the per-query top-10 kept by the kernel (reranking)
+    topk = None
+    if kind in ("single", "batched") and world == 1 and not args.no_topk:
+        topk = time_topk(args, w, dev, 10, out_for_check)
+
     # end to end through the public API from pinned host memory
     e2e = None if args.no_e2e else run_e2e(args, w, fm, sharded, world, dev)
 
@@ -469,13 +474,62 @@ def run_config(args, cfg, rank, world, dev, headline: bool) -> dict:
                    f"documents rotated over {w.n_copies} copies ({w.n_copies * w.in_bytes / 1e6:.0f} MB > 4x L2) "
                    "between steps"},
         "roofline": roof, "kernel_ms": round(kern_avg_ms, 4), "clocks": clocks, "parity": par,
-        "e2e": e2e, "cpu_baseline": cpu, "reference_gpu": ref_gpu,
+        "e2e": e2e, "cpu_baseline": cpu, "reference_gpu": ref_gpu, "topk": topk,
         "gpu_launches": args.steps * (3 if kind == "train" else 1),
     }
     del w, graphs, graph_out, out_for_check
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
     return res
+
+
+def time_topk(args, w: Workload, dev, k: int, full_out):
+    """flash_maxsim(_batched)_topk on the same documents: device time per
+    call (graph replay, documents rotated like the main step) and whether
+    its ids are exactly the stable top-k of the full scores."""
+    import flash_maxsim_b200 as fm
+
+    def call(i):
+        if w.kind == "single":
+            return fm.flash_maxsim_topk(w.Q, w.D_copies[i], k)
+        return fm.flash_maxsim_batched_topk(w.Q, w.D_copies[i], k)
+
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for i in range(w.n_copies):
+            call(i)
+    stream.wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graphs, outs = [], []
+    for i in range(w.n_copies):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs.append(call(i))
+        graphs.append(g)
+    for j in range(args.warmup):
+        graphs[j % w.n_copies].replay()
+    torch.cuda.synchronize(dev)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for j in range(args.steps):
+        graphs[j % w.n_copies].replay()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    fm.check_status(dev)
+    ms = a.elapsed_time(b) / args.steps
+    v, i = outs[0]
+    full = full_out if full_out.dim() == 2 else full_out.unsqueeze(0)
+    v2 = v if v.dim() == 2 else v.unsqueeze(0)
+    i2 = i if i.dim() == 2 else i.unsqueeze(0)
+    # stable order: score descending, then id ascending
+    o1 = torch.argsort(full, dim=1, descending=True, stable=True)[:, :k]
+    exact = bool(torch.equal(o1, i2) and torch.equal(torch.gather(full, 1, o1), v2))
+    return {"k": k, "value": round(w.units() / (ms / 1e3), 1), "unit": w.unit_name(), "ms_per_step": round(ms, 4),
+            "ids_equal_stable_topk_of_full_scores": exact,
+            "launches_per_step": 2}
 
 
 def run_e2e(args, w: Workload, fm, sharded, world, dev):
@@ -766,6 +820,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-topk", action="store_true", help="skip timing the top-k variant")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's Triton kernels")
     ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly (no CUDA graph)")
     for name in ("nq", "lq", "ld", "dim"):
