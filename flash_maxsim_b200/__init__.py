@@ -12,6 +12,8 @@ from .api import (  # noqa: F401
     flash_maxsim_batched,
     flash_maxsim_topk,
     flash_maxsim_batched_topk,
+    flash_maxsim_packed,
+    pack_documents,
     topk_scores,
     flash_maxsim_train,
     maxsim_naive,
@@ -27,6 +29,8 @@ __all__ = [
     "flash_maxsim_batched",
     "flash_maxsim_topk",
     "flash_maxsim_batched_topk",
+    "flash_maxsim_packed",
+    "pack_documents",
     "topk_scores",
     "flash_maxsim_train",
     "maxsim_naive",

@@ -36,6 +36,7 @@ SIGNATURES = {
     "fm_set_wait_timeout_ns": (None, [_I64]),
     "fm_set_option": (_I, [_I, _I]),
     "fm_maxsim_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "fm_maxsim_packed_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I64, _P, _P]),
     "fm_maxsim_int8_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_sparse_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "fm_maxsim_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64, _P]),

@@ -154,6 +154,62 @@ def flash_maxsim_batched(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None,
 
 
 # ---------------------------------------------------------------------------
+# packed (unpadded) documents
+# ---------------------------------------------------------------------------
+
+def flash_maxsim_packed(Q: torch.Tensor, D_tokens: torch.Tensor, cu_seqlens, max_len: int | None = None):
+    """MaxSim over packed documents: document b is rows
+    cu_seqlens[b]:cu_seqlens[b+1] of D_tokens [T, d] (ragged encoder output
+    concatenated, no padding). Q: [Lq, d] -> [B] or [Nq, Lq, d] -> [Nq, B] fp32.
+
+    Equal to flash_maxsim(_batched) on the same documents padded to
+    [B, max_len, d] with doc_lengths = diff(cu_seqlens). `max_len` must bound
+    every length (None: computed here, which synchronises with the device)."""
+    assert Q.dim() in (2, 3) and D_tokens.dim() == 2 and Q.shape[-1] == D_tokens.shape[1]
+    _require_cuda(Q, D_tokens)
+    single = Q.dim() == 2
+    Q3 = Q.unsqueeze(0) if single else Q
+    Nq, Lq, d = Q3.shape
+    cu = cu_seqlens if torch.is_tensor(cu_seqlens) else torch.as_tensor(cu_seqlens)
+    cu = cu.to(device=D_tokens.device, dtype=torch.int32).contiguous()
+    assert cu.dim() == 1 and cu.numel() >= 1
+    B = cu.numel() - 1
+    T = D_tokens.shape[0]
+    dev = D_tokens.device
+    if max_len is None:
+        max_len = int((cu[1:] - cu[:-1]).max().item()) if B > 0 else 1
+    max_len = max(int(max_len), 1)
+    if B == 0 or Nq == 0:
+        out = torch.empty(Nq, B, device=dev, dtype=torch.float32)
+        return out.squeeze(0) if single else out
+    if Lq == 0 or T == 0:
+        out = _degenerate(Nq, B, Lq, 0 if T == 0 else max_len, dev)
+        return out.squeeze(0) if single else out
+    Qh, Dh = _half(Q3), _half(D_tokens)
+    scores = torch.empty(Nq, B, device=dev, dtype=torch.float32)
+    _before_call(dev)
+    with _lib.on_device(dev):
+        rc = lib.fm_maxsim_packed_fwd(Qh.data_ptr(), Dh.data_ptr(), cu.data_ptr(), scores.data_ptr(), None,
+                                      Nq, B, Lq, max_len, Qh.shape[-1], T, _lib.status_word(dev).data_ptr(),
+                                      _lib.stream_of(dev))
+    _lib.check(rc, "fm_maxsim_packed_fwd")
+    _after_call(dev)
+    return scores.squeeze(0) if single else scores
+
+
+def pack_documents(D: torch.Tensor, doc_lengths):
+    """Padded [B, Ld, d] documents + lengths -> (D_tokens [sum(len), d],
+    cu_seqlens int32 [B + 1]): the packed layout flash_maxsim_packed reads."""
+    assert D.dim() == 3
+    B, Ld, d = D.shape
+    lens = torch.as_tensor(doc_lengths, device=D.device).to(torch.int64).clamp(0, Ld)
+    cu = torch.zeros(B + 1, dtype=torch.int64, device=D.device)
+    cu[1:] = torch.cumsum(lens, 0)
+    mask = torch.arange(Ld, device=D.device)[None, :] < lens[:, None]
+    return D[mask].contiguous(), cu.to(torch.int32)
+
+
+# ---------------------------------------------------------------------------
 # top-k (callers of the reference: examples/demo.py:126-134, benchmarks/bench.py:36)
 # ---------------------------------------------------------------------------
 

@@ -301,14 +301,16 @@ bool flat_ok(const Shape& s, const int32_t* lengths);
 int launch_flat(const Shape& s, const void* Q, const void* D, float* scores, int32_t* status,
                 cudaStream_t stream);
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
-              const int32_t* sp_idx, int32_t* status, cudaStream_t stream, TopkArgs* topk);
+              const int32_t* sp_idx, int32_t* status, cudaStream_t stream, TopkArgs* topk,
+              const int32_t* cu, int64_t T);
 
 // Forward launch for any shape.  `topk` (optional): when the chosen kernel
 // selects per-CTA top-k candidates in its tail (one query or shared dense
 // documents), topk->parts is set to its grid; otherwise it stays 0.
 int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
                int32_t* argmax, const int32_t* sp_idx, const void* scales, const void* mins,
-               int32_t* status, cudaStream_t stream, TopkArgs* topk = nullptr) {
+               int32_t* status, cudaStream_t stream, TopkArgs* topk = nullptr,
+               const int32_t* cu = nullptr, int64_t T = 0) {
   if (!Q || !D || !scores || !status) return FM_ERR_ARG;
   if (s.Nq < 1 || s.B < 0 || s.Lq < 1 || s.Ld < 1 || s.d < 8 || s.d > 2048) return FM_ERR_ARG;
   if (s.d % 8 != 0) return FM_ERR_ARG;
@@ -321,13 +323,15 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   if (n_docs > INT32_MAX || static_cast<int64_t>(s.Nq) * s.B > INT32_MAX) return FM_ERR_ARG;
 
   if (topk) topk->parts = 0;
-  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, sp_idx, status, stream, topk);
-  if (!topk && flat_ok(s, lengths)) return launch_flat(s, Q, D, scores, status, stream);
+  if (cu && (s.mode != MODE_DENSE || !s.shared || T < 1 || T >= INT32_MAX)) return FM_ERR_ARG;
+  if (q1_ok(s)) return launch_q1(s, Q, D, lengths, scores, sp_idx, status, stream, topk, cu, T);
+  if (!topk && !cu && flat_ok(s, lengths)) return launch_flat(s, Q, D, scores, status, stream);
 
   FwdArgs a{};
   int smem = 0;
   if (!make_plan(s, a, smem)) return FM_ERR_UNSUPPORTED;
   a.lengths = lengths;
+  a.cu = cu;
   a.scores = scores;
   a.argmax = argmax;
   a.sp_idx = sp_idx;
@@ -356,6 +360,11 @@ int fwd_common(const Shape& s, const void* Q, const void* D, const int32_t* leng
   if (s.mode == MODE_INT8) {
     if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, s.d, s.Ld, n_docs, 64, a.C,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
+      return FM_ERR_LAUNCH;
+  } else if (cu) {
+    // packed documents: one [T, d] token matrix, rows addressed through cu
+    if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, static_cast<uint64_t>(T), 1, 64, a.C,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
       return FM_ERR_LAUNCH;
   } else {
     if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, s.Ld, n_docs, 64, a.C,
@@ -515,12 +524,14 @@ int launch_q1_t(const CUtensorMap& tq, const CUtensorMap& td, const Q1Args& a, i
 }
 
 int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengths, float* scores,
-              const int32_t* sp_idx, int32_t* status, cudaStream_t stream, TopkArgs* topk) {
+              const int32_t* sp_idx, int32_t* status, cudaStream_t stream, TopkArgs* topk,
+              const int32_t* cu, int64_t T) {
   const int CT = tune().C == 256 ? 256 : 128;
   Q1Args a{};
   int smem = 0;
   if (!plan_q1(s, CT, a, smem)) return FM_ERR_UNSUPPORTED;
   a.lengths = lengths;
+  a.cu = cu;
   a.scores = scores;
   a.status = status;
   a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
@@ -539,8 +550,10 @@ int launch_q1(const Shape& s, const void* Q, const void* D, const int32_t* lengt
   if (!make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Q, s.d, s.Lq, 1, 64, a.N,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return FM_ERR_LAUNCH;
-  if (!make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, s.Ld, s.B, 64, CT,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!(cu ? make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, static_cast<uint64_t>(T), 1, 64, CT,
+                         CU_TENSOR_MAP_SWIZZLE_128B)
+           : make_map_3d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, s.d, s.Ld, s.B, 64, CT,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return FM_ERR_LAUNCH;
   if (a.N == 32)
     return CT == 256 ? launch_q1_t<1, 256>(tq, td, a, smem, stream) : launch_q1_t<1, 128>(tq, td, a, smem, stream);
@@ -687,6 +700,15 @@ int fm_maxsim_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengt
   Shape s{MODE_DENSE, argmax != nullptr, Nq, B, Lq, Ld, d, 0, shared_docs ? 1 : 0};
   return fwd_common(s, Q, D, doc_lengths, scores, argmax, nullptr, nullptr, nullptr, status,
                     static_cast<cudaStream_t>(stream));
+}
+
+int fm_maxsim_packed_fwd(const uint16_t* Q, const uint16_t* D_tokens, const int32_t* cu_seqlens,
+                         float* scores, int32_t* argmax, int Nq, int B, int Lq, int max_len, int d,
+                         int64_t total_tokens, int32_t* status, void* stream) {
+  if (!cu_seqlens) return FM_ERR_ARG;
+  Shape s{MODE_DENSE, argmax != nullptr, Nq, B, Lq, max_len, d, 0, 1};
+  return fwd_common(s, Q, D_tokens, nullptr, scores, argmax, nullptr, nullptr, nullptr, status,
+                    static_cast<cudaStream_t>(stream), nullptr, cu_seqlens, total_tokens);
 }
 
 int fm_maxsim_int8_fwd(const uint16_t* Q, const uint8_t* D_u8, const uint16_t* scales,

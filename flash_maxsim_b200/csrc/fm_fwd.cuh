@@ -61,6 +61,7 @@ constexpr int kMaxGroupDocs = 8;
 
 struct FwdArgs {
   const int32_t* lengths;    // [n_docs] valid tokens per doc, or null (all Ld)
+  const int32_t* cu;         // packed documents: [n_docs + 1] token offsets into D [T, d], or null
   float* scores;             // [Nq, B] (dense), [B] (sparse / int8)
   int32_t* argmax;           // [Nq*B, Lq] or null
   const int32_t* sp_idx;     // sparse: [B, K]
@@ -111,7 +112,7 @@ struct Ring {
 };
 
 __device__ __forceinline__ int doc_len(const FwdArgs& a, int doc) {
-  int len = a.lengths ? __ldg(a.lengths + doc) : a.Ld;
+  int len = a.cu ? __ldg(a.cu + doc + 1) - __ldg(a.cu + doc) : (a.lengths ? __ldg(a.lengths + doc) : a.Ld);
   return len < 0 ? 0 : (len > a.Ld ? a.Ld : len);
 }
 
@@ -446,8 +447,13 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 FM_TR(4, 2);
                 mbar_expect_tx(full, tx);
                 const uint32_t dst = ring_base + r.idx * slot_bytes;
+                // padded documents: (token, doc) of a [docs, Ld, d] map; packed
+                // documents: row cu[doc] + token of a [T, d] map (rows of the next
+                // document past the end are masked by the epilogue)
+                const int row = (a.cu ? __ldg(a.cu + doc) : 0) + c * a.C;
+                const int zc = a.cu ? 0 : doc;
                 for (int at = 0; at < a.d_atoms_real; ++at)
-                  tma_load_3d(dst + at * atom_bytes, &tmap_d, at * 64, c * a.C, doc, full, pol);
+                  tma_load_3d(dst + at * atom_bytes, &tmap_d, at * 64, row, zc, full, pol);
                 FM_TR(4, 3);
                 r.next(nslots);
                 ++issued;

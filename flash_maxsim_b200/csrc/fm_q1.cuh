@@ -41,6 +41,7 @@ constexpr int kQ1Xch = 8;  // per-document exchange slots of the epilogue
 
 struct Q1Args {
   const int32_t* lengths;  // [B] or null
+  const int32_t* cu;       // packed documents: [B + 1] token offsets into D [T, d], or null
   float* scores;           // [B]
   int* status;
   uint64_t timeout_ns;
@@ -58,7 +59,7 @@ struct Q1Args {
 };
 
 __device__ __forceinline__ int q1_len(const Q1Args& a, int b) {
-  int len = a.lengths ? __ldg(a.lengths + b) : a.Ld;
+  int len = a.cu ? __ldg(a.cu + b + 1) - __ldg(a.cu + b) : (a.lengths ? __ldg(a.lengths + b) : a.Ld);
   return len < 0 ? 0 : (len > a.Ld ? a.Ld : len);
 }
 
@@ -177,8 +178,10 @@ __global__ void __launch_bounds__(q1_threads(EW), 1)
           }
           mbar_expect_tx(u_full(ur.idx), tx);
           const uint32_t dst = sbase + a.off_u + ur.idx * a.u_slot_bytes;
+          const int row = (a.cu ? __ldg(a.cu + b) : 0) + c * CT;  // packed: row of a [T, d] map
+          const int zc = a.cu ? 0 : b;
           for (int at = 0; at < a.atoms; ++at)
-            tma_load_3d(dst + at * CT * 128, &tmap_d, at * 64, c * CT, b, u_full(ur.idx), pol);
+            tma_load_3d(dst + at * CT * 128, &tmap_d, at * 64, row, zc, u_full(ur.idx), pol);
           ur.next(a.nu);
           ++issued;
         }

@@ -102,6 +102,25 @@ int fm_maxsim_fwd(const uint16_t* Q, const uint16_t* D, const int32_t* doc_lengt
                   int shared_docs, int32_t* status, void* stream);
 
 /*
+ * MaxSim forward over packed (unpadded) documents: document b is rows
+ * [cu_seqlens[b], cu_seqlens[b+1]) of D_tokens [total_tokens, d] fp16, so a
+ * ragged batch needs no padding in host or device memory.
+ *   scores[n * B + b] = sum_{q<Lq} max_{cu[b] <= t < cu[b+1]} <Q[n,q,:], D_tokens[t,:]>
+ * cu_seqlens: int32 [B + 1], non-decreasing, cu[0] >= 0, cu[B] <= total_tokens.
+ * max_len: an upper bound of every document's length (longer documents are
+ *   cut to max_len tokens, as doc_lengths > Ld are clamped to Ld); it sizes
+ *   the launch plan. An empty document scores -inf.
+ * argmax: NULL, or int32 [Nq*B, Lq] (token index within the document).
+ * Q: [Nq, Lq, d] fp16, shared by every document. Same kernels as
+ * fm_maxsim_fwd (the TMA box of a chunk starts at the document's first row).
+ * No counterpart in the reference, whose callers pad ragged documents to
+ * [B, Ld, d] with doc_lengths (examples/demo.py:55-69).
+ */
+int fm_maxsim_packed_fwd(const uint16_t* Q, const uint16_t* D_tokens, const int32_t* cu_seqlens,
+                         float* scores, int32_t* argmax, int Nq, int B, int Lq, int max_len, int d,
+                         int64_t total_tokens, int32_t* status, void* stream);
+
+/*
  * Fused dequantise + MaxSim, single query.
  *   scores[b] = sum_q max_t sum_k Q[q,k] * (u[b,t,k] * scale[b,t] + min[b,t])
  * D_u8: [B, Ld, d] uint8 (d % 16 == 0), scales/mins: [B, Ld] fp16.
