@@ -62,6 +62,8 @@ CONFIGS = {
            "batched"),
     "c4": ("INT8 fused-dequant MaxSim Q[32,128] x u8 D[200000,300,128] + scale/min", 1, 32, 200000, 300,
            128, "int8"),
+    "c4fp8": ("FP8 e4m3 documents (per-token fp32 scale) MaxSim Q[32,128] x e4m3 D[200000,300,128]", 1, 32,
+              200000, 300, 128, "fp8"),
     "c5": ("varlen train fwd+bwd Q[64,64,256] x D[4096,1024,256], lengths U[32,1024]", 64, 64, 4096, 1024,
            256, "train"),
 }
@@ -225,7 +227,7 @@ class Workload:
         self.Nq, self.Lq, self.B, self.Ld, self.d = Nq, Lq, B, Ld, d
         lo, hi = shard(B, rank, world)
         self.lo, self.Bl = lo, hi - lo
-        self.Q = synth((Nq, Lq, d) if kind not in ("single", "int8") else (Lq, d), 1, dev)
+        self.Q = synth((Nq, Lq, d) if kind not in ("single", "int8", "fp8") else (Lq, d), 1, dev)
         D = synth((self.Bl, Ld, d), 1000 + rank, dev)
         self.lengths = None
         if kind == "train":
@@ -237,12 +239,22 @@ class Workload:
             del D
             D = None
             torch.cuda.empty_cache()
+        if kind == "fp8":
+            self.Du8, self.sc = fm.quantize_fp8(D)
+            self.mn = torch.empty(0, device=dev)
+            del D
+            D = None
+            torch.cuda.empty_cache()
         self.D = D
         self.grad = None
         if kind == "train":
             self.grad = torch.randn(Nq, self.Bl, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
-        self.in_bytes = ((self.Du8.numel() + self.sc.numel() * 2 + self.mn.numel() * 2) if kind == "int8"
-                         else D.numel() * 2)
+        if kind == "int8":
+            self.in_bytes = self.Du8.numel() + self.sc.numel() * 2 + self.mn.numel() * 2
+        elif kind == "fp8":
+            self.in_bytes = self.Du8.numel() + self.sc.numel() * 4
+        else:
+            self.in_bytes = D.numel() * 2
         # inputs smaller than 4x L2: rotate over enough copies of the documents
         # that every step reads its batch from HBM (no step finds it in L2)
         self.n_copies = 1
@@ -261,6 +273,8 @@ class Workload:
         if self.kind == "batched":
             return fm.flash_maxsim_batched(self.Q, self.D_copies[i])
         u, s_, m_ = self.U_copies[i]
+        if self.kind == "fp8":
+            return fm.flash_maxsim_fp8(self.Q, u, s_)
         return fm.flash_maxsim_int8(self.Q, u, s_, m_)
 
     def units(self):
@@ -288,6 +302,10 @@ def parity(w: Workload, out, dev) -> dict:
         idx = SC.sample_docs(w.Bl, 256, seed=11)
         it = torch.from_numpy(idx).to(dev)
         res = SC.check_int8(npy(w.Q), npy(w.Du8[it]), npy(w.sc[it]), npy(w.mn[it]), npy(out[it]))
+    elif w.kind == "fp8":
+        idx = SC.sample_docs(w.Bl, 256, seed=11)
+        it = torch.from_numpy(idx).to(dev)
+        res = SC.check_fp8(npy(w.Q), npy(w.Du8[it].view(torch.float8_e4m3fn).float()), npy(w.sc[it]), npy(out[it]))
     else:
         from flash_maxsim_b200 import api
         Qg = w.Q.detach().clone().requires_grad_(True)
@@ -416,7 +434,7 @@ def run_config(args, cfg, rank, world, dev, headline: bool) -> dict:
     flops = 2.0 * Nq * Lq * Ld * d * Bl
     if kind == "train":
         flops = 2.0 * Nq * Lq * float(w.lengths.sum().item()) * d
-    if kind in ("single", "int8"):
+    if kind in ("single", "int8", "fp8"):
         alg_bytes = w.in_bytes + w.Q.numel() * 2 + Bl * 4
         achieved = alg_bytes / (kern_avg_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -540,6 +558,9 @@ def run_e2e(args, w: Workload, fm, sharded, world, dev):
     if kind == "int8":
         hD = [w.Du8.cpu().pin_memory(), w.sc.cpu().pin_memory(), w.mn.cpu().pin_memory()]
         dD = [torch.empty_like(w.Du8), torch.empty_like(w.sc), torch.empty_like(w.mn)]
+    elif kind == "fp8":
+        hD = [w.Du8.cpu().pin_memory(), w.sc.cpu().pin_memory()]
+        dD = [torch.empty_like(w.Du8), torch.empty_like(w.sc)]
     else:
         hD = [w.D.cpu().pin_memory()]
         dD = [torch.empty_like(w.D)]
@@ -562,6 +583,8 @@ def run_e2e(args, w: Workload, fm, sharded, world, dev):
             out = fm.flash_maxsim_batched(q, dD[0])
         elif kind == "int8":
             out = fm.flash_maxsim_int8(q, dD[0], dD[1], dD[2])
+        elif kind == "fp8":
+            out = fm.flash_maxsim_fp8(q, dD[0], dD[1])
         else:
             qg = q.requires_grad_(True)
             dg = dD[0].requires_grad_(True)
@@ -618,6 +641,8 @@ def reference_gpu(args, w: Workload, dev):
     ref = reference_module()
     if ref is None:
         return {"unavailable": "reference package not installed under baseline/_ref"}
+    if w.kind == "fp8":
+        return {"unavailable": "the reference has no FP8 document format (its quantised path is INT8)"}
     if w.kind == "train":
         return {"unavailable": "the reference's training path takes one query and no doc_lengths "
                                "(flash_maxsim/flash_maxsim.py:253-291)"}
@@ -696,7 +721,7 @@ def cpu_baseline(cfg: str, seconds: float):
     from oracle import maxsim_oracle as O
     desc, Nq, Lq, B, Ld, d, kind = CONFIGS[cfg]
     n_docs = _cpu_sample_docs(kind, Lq, Ld, d)
-    nq = 1 if kind in ("single", "int8") else min(Nq, 4)
+    nq = 1 if kind in ("single", "int8", "fp8") else min(Nq, 4)
     Q, D = O.seeded_inputs(123, (nq, Lq, d), (n_docs, Ld, d))
     lens = None
     if kind == "train":
@@ -704,6 +729,8 @@ def cpu_baseline(cfg: str, seconds: float):
     if kind == "int8":
         u8, s, m = O.quantize_int8(D)
         D = O.dequantize_int8(u8, s, m)
+    if kind == "fp8":
+        D = O.dequantize_fp8(*O.quantize_fp8(D))
     threads = os.cpu_count() or 1
     ref = reference_module()
     old_threads = torch.get_num_threads()
@@ -796,7 +823,7 @@ def run_ours(args):
             "data": "synthetic N(0,1), rows L2-normalised, seeded",
             "config": head["config"], "roofline": head["roofline"], "cpu_baseline": head["cpu_baseline"],
             "e2e": head["e2e"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
-            "parity": head["parity"], "reference_gpu": head["reference_gpu"],
+            "parity": head["parity"], "reference_gpu": head["reference_gpu"], "topk": head["topk"],
         }
         if extras:
             line["configs"] = extras
@@ -812,7 +839,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS), help="headline configuration")
-    ap.add_argument("--extra", default="c1,c3,c4,c5",
+    ap.add_argument("--extra", default="c1,c3,c4,c4fp8,c5",
                     help="further configurations measured in the same run at N=1 (empty: none)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=3)

@@ -20,6 +20,9 @@ from .api import (  # noqa: F401
     flash_maxsim_int8,
     quantize_int8,
     dequantize_int8,
+    flash_maxsim_fp8,
+    quantize_fp8,
+    dequantize_fp8,
     flash_maxsim_sparse,
     maxsim_sparse_naive,
 )
@@ -37,6 +40,9 @@ __all__ = [
     "flash_maxsim_int8",
     "quantize_int8",
     "dequantize_int8",
+    "flash_maxsim_fp8",
+    "quantize_fp8",
+    "dequantize_fp8",
     "flash_maxsim_sparse",
     "maxsim_sparse_naive",
     "check_status",

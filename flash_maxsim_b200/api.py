@@ -479,6 +479,76 @@ def flash_maxsim_int8(Q: torch.Tensor, D_uint8: torch.Tensor, scales: torch.Tens
 
 
 # ---------------------------------------------------------------------------
+# FP8 (e4m3) document storage: the INT8 path's sibling with one scale per token
+# ---------------------------------------------------------------------------
+
+def quantize_fp8(D: torch.Tensor):
+    """Per-token e4m3 quantisation on the GPU: D [B, Ld, d] (fp16 / bf16 /
+    fp32) -> (codes uint8 [B, Ld, d] holding e4m3 bit patterns, scales fp32
+    [B, Ld, 1]) with scale = max|x| / 448 (1 for an all-zero token) and
+    code = e4m3(x / scale), round-to-nearest-even."""
+    assert D.dim() == 3
+    _require_cuda(D)
+    B, Ld, d = D.shape
+    x = D if D.dtype in _QDTYPE else D.float()
+    pad = (-d) % 8
+    if pad:
+        x = F.pad(x, (0, pad))  # zeros change no row's max |x|
+    x = _aligned(x)
+    dp = d + pad
+    codes = torch.empty(B, Ld, dp, device=D.device, dtype=torch.uint8)
+    scales = torch.empty(B, Ld, 1, device=D.device, dtype=torch.float32)
+    rows = B * Ld
+    if rows:
+        _before_call(D.device)
+        with _lib.on_device(D.device):
+            rc = lib.fm_quantize_fp8(x.data_ptr(), _QDTYPE[x.dtype], codes.data_ptr(), scales.data_ptr(), rows, dp,
+                                     _lib.stream_of(D.device))
+        _lib.check(rc, "fm_quantize_fp8")
+        _after_call(D.device)
+    if pad:
+        codes = codes[..., :d].contiguous()
+    return codes, scales
+
+
+def dequantize_fp8(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Reconstruct fp32 values e4m3(code) * scale (plain torch)."""
+    return codes.view(torch.float8_e4m3fn).float() * scales.float()
+
+
+def flash_maxsim_fp8(Q: torch.Tensor, D_fp8: torch.Tensor, scales: torch.Tensor, doc_lengths=None) -> torch.Tensor:
+    """MaxSim on e4m3 documents. Q: [Lq, d] (Lq <= 64), D_fp8: uint8 [B, Ld, d]
+    e4m3 codes, scales: [B, Ld, 1] or [B, Ld] -> [B] fp32, equal to
+    maxsim_naive(Q, dequantize_fp8(D_fp8, scales)) within fp32 rounding."""
+    assert Q.dim() == 2 and D_fp8.dim() == 3 and Q.shape[1] == D_fp8.shape[2]
+    _require_cuda(Q, D_fp8, scales)
+    Lq, d = Q.shape
+    B, Ld, _ = D_fp8.shape
+    assert Lq <= 64, "the FP8 path scores queries of at most 64 tokens"
+    if scales.dim() == 3:
+        scales = scales.squeeze(-1)
+    lengths = _lengths(doc_lengths, B, Ld, D_fp8.device)
+    if Lq == 0 or Ld == 0:
+        return _degenerate(1, B, Lq, Ld, D_fp8.device).squeeze(0)
+    Qh = _half(Q, 16)
+    Du = _aligned(_pad_last(D_fp8.view(torch.uint8) if D_fp8.dtype != torch.uint8 else D_fp8, 16))
+    sc = _aligned(scales.float())
+    assert sc.shape == (B, Ld)
+    assert Qh.shape[-1] <= 256, "the FP8 path supports d <= 256"
+    scores = torch.empty(B, device=Q.device, dtype=torch.float32)
+    if B == 0:
+        return scores
+    dev = Q.device
+    _before_call(dev)
+    with _lib.on_device(dev):
+        rc = lib.fm_maxsim_fp8_fwd(Qh.data_ptr(), Du.data_ptr(), sc.data_ptr(), _lib.ptr(lengths), scores.data_ptr(),
+                                   B, Lq, Ld, Qh.shape[-1], _lib.status_word(dev).data_ptr(), _lib.stream_of(dev))
+    _lib.check(rc, "fm_maxsim_fp8_fwd")
+    _after_call(dev)
+    return scores
+
+
+# ---------------------------------------------------------------------------
 # sparse (flash_maxsim/flash_maxsim_sparse.py)
 # ---------------------------------------------------------------------------
 

@@ -19,6 +19,7 @@
 #include "fm_q1.cuh"
 #include "fm_flat.cuh"
 #include "fm_topk.cuh"
+#include "fm_fp8.cuh"
 
 // Scratch for fm_maxsim_bwd_noalloc: the dQ partial sums live here instead of
 // in caller-provided memory.  Every device that loads this library keeps
@@ -637,6 +638,77 @@ int launch_flat(const Shape& s, const void* Q, const void* D, float* scores, int
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
+// FP8 path (fm_fp8.cuh): one query of <= 64 rows, e4m3 documents, d <= 256.
+bool plan_fp8(int B, int Lq, int Ld, int d, Fp8Args& a, int& smem) {
+  a.B = B;
+  a.Lq = Lq;
+  a.Ld = Ld;
+  a.d = d;
+  const int gq = cdiv(Lq, 32);
+  a.N = kF8Parts * 32 * gq;
+  a.nts = (512 / a.N) & ~1;  // even: the two warps of a lane quarter own alternate slots
+  if (a.nts < 2) return false;
+  a.atoms = cdiv(d, 128);
+  a.u_slot_bytes = a.atoms * kF8Tokens * 128u;
+  const int q_bytes = round_up(a.atoms * a.N * 128, 1024);
+  const int misc = round_up((64 + kF8Xch * kF8EW * gq * 32) * 4 + 2 * kF8Xch * 4, 16);
+  const int fixed = 1024 + q_bytes + misc + (2 * 16 + 2 * a.nts + 2) * 8 + 32;
+  a.nu = std::min(16, (kMaxSmem - fixed) / static_cast<int>(a.u_slot_bytes));
+  if (a.nu < 2) return false;
+  uint32_t off = 0;
+  a.off_q = off;
+  off += q_bytes;
+  a.off_u = off;
+  off += a.nu * a.u_slot_bytes;
+  a.off_misc = round_up(off, 16);
+  off = a.off_misc + misc;
+  a.off_bar = round_up(off, 16);
+  off = a.off_bar + (2 * a.nu + 2 * a.nts + 2) * 8 + 32;
+  smem = std::max(static_cast<int>(off) + 1024, kMinSmem);
+  return smem <= kMaxSmem;
+}
+
+template <int GQ>
+int launch_fp8_gq(const CUtensorMap& tu, const Fp8Args& a, int smem, cudaStream_t stream) {
+  static std::atomic<bool> cfg{false};
+  if (!cfg.load()) {
+    if (cudaFuncSetAttribute(maxsim_fp8_kernel<GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+        cudaSuccess)
+      return FM_ERR_LAUNCH;
+    cfg.store(true);
+  }
+  const int sms = sm_count();
+  if (sms <= 0) return FM_ERR_NO_DEVICE;
+  maxsim_fp8_kernel<GQ><<<std::max(1, std::min(a.B, sms)), f8_threads(), smem, stream>>>(tu, a);
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+int launch_fp8(const void* Q, const void* D8, const float* scales, const int32_t* lengths, float* scores, int B,
+               int Lq, int Ld, int d, int32_t* status, cudaStream_t stream, TopkArgs* topk) {
+  Fp8Args a{};
+  int smem = 0;
+  if (!plan_fp8(B, Lq, Ld, d, a, smem)) return FM_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(scales) & 3u) != 0) return FM_ERR_ARG;
+  a.lengths = lengths;
+  a.scores = scores;
+  a.q = static_cast<const __half*>(Q);
+  a.scales = scales;
+  a.status = status;
+  a.timeout_ns = static_cast<uint64_t>(g_timeout_ns.load());
+  a.topk = TopkArgs{0, 0, nullptr, nullptr};
+  if (topk && topk->k > 0) {
+    const int sms = sm_count();
+    if (sms <= 0) return FM_ERR_NO_DEVICE;
+    topk->parts = std::max(1, std::min(B, sms));
+    a.topk = *topk;
+  }
+  CUtensorMap tu;
+  if (!make_map_3d(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D8, d, Ld, B, 128, kF8Tokens,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return FM_ERR_LAUNCH;
+  return a.N == 96 ? launch_fp8_gq<1>(tu, a, smem, stream) : launch_fp8_gq<2>(tu, a, smem, stream);
+}
+
 }  // namespace
 }  // namespace fm
 
@@ -796,6 +868,42 @@ int dq_splits(int Nq, int B, int Lq, int Ld, int d) {
 }  // namespace fm
 
 extern "C" {
+
+int fm_maxsim_fp8_fwd(const uint16_t* Q, const uint8_t* D_fp8, const float* scales, const int32_t* doc_lengths,
+                      float* scores, int B, int Lq, int Ld, int d, int32_t* status, void* stream) {
+  if (!Q || !D_fp8 || !scales || !scores || !status || B < 0 || Lq < 1 || Lq > 64 || Ld < 1 || d < 16 ||
+      d > 256 || d % 16 != 0)
+    return FM_ERR_ARG;
+  if (!aligned16(Q) || !aligned16(D_fp8)) return FM_ERR_ARG;
+  if (B == 0) return FM_OK;
+  return launch_fp8(Q, D_fp8, scales, doc_lengths, scores, B, Lq, Ld, d, status, static_cast<cudaStream_t>(stream),
+                    nullptr);
+}
+
+int fm_quantize_fp8(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d, void* stream) {
+  if (!D || !D_fp8 || !scales || rows < 0 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
+  if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_fp8) & 7u)) return FM_ERR_ARG;
+  if (rows == 0) return FM_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > INT32_MAX) return FM_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned nb = static_cast<unsigned>(blocks);
+  switch (dtype) {
+    case FM_DTYPE_F16:
+      quantize_fp8_kernel<__half><<<nb, 256, 0, st>>>(static_cast<const __half*>(D), D_fp8, scales, rows, d);
+      break;
+    case FM_DTYPE_F32:
+      quantize_fp8_kernel<float><<<nb, 256, 0, st>>>(static_cast<const float*>(D), D_fp8, scales, rows, d);
+      break;
+    case FM_DTYPE_BF16:
+      quantize_fp8_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(D), D_fp8, scales,
+                                                               rows, d);
+      break;
+    default:
+      return FM_ERR_ARG;
+  }
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
 
 int64_t fm_topk_workspace_size(int Nq, int k) {
   if (Nq < 1 || k < 1 || k > kTopkMaxK) return 0;

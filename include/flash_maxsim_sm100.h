@@ -132,6 +132,21 @@ int fm_maxsim_int8_fwd(const uint16_t* Q, const uint8_t* D_u8, const uint16_t* s
                        int Lq, int Ld, int d, int32_t* status, void* stream);
 
 /*
+ * FP8 document storage: e4m3 codes [B, Ld, d] (d % 16 == 0, d <= 256) with
+ * one fp32 scale per token [B, Ld], single query of Lq <= 64 rows.
+ *   scores[b] = sum_q max_{t<len(b)} sum_k Q[q,k] * scale[b,t] * e4m3(D_fp8[b,t,k])
+ * Half the bytes of fp16 documents. The sibling of fm_maxsim_int8_fwd
+ * (which replaces flash_maxsim/flash_maxsim_quant.py:105-142); the reference
+ * has no FP8 format.
+ * fm_quantize_fp8: rows of d elements of type `dtype` (FM_DTYPE_*) ->
+ *   scale = max|x| / 448 (1 for an all-zero row), code = e4m3(x / scale),
+ *   round-to-nearest-even, saturating; D_fp8 [rows, d] bytes, scales fp32 [rows].
+ */
+int fm_maxsim_fp8_fwd(const uint16_t* Q, const uint8_t* D_fp8, const float* scales, const int32_t* doc_lengths,
+                      float* scores, int B, int Lq, int Ld, int d, int32_t* status, void* stream);
+int fm_quantize_fp8(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d, void* stream);
+
+/*
  * Sparse MaxSim: per document b, only the K query rows indices[b, :] count
  * (duplicates count twice, negative indices wrap like torch indexing).
  *   scores[b] = sum_{k<K} max_{t<len(b)} <Q[indices[b,k],:], D[b,t,:]>

@@ -136,6 +136,37 @@ def dequantize_int8(u8, scales, mins) -> np.ndarray:
             + np.asarray(mins).astype(np.float32))
 
 
+def e4m3_round(x) -> np.ndarray:
+    """Round fp32 values to the nearest e4m3 (fn variant: 4 exponent bits,
+    bias 7, 3 mantissa bits, subnormal step 2**-9, largest finite 448, no
+    infinities), ties to even, saturating at +-448; returned as fp32."""
+    x = np.asarray(x, dtype=np.float32)
+    ax = np.abs(x).astype(np.float64)
+    with np.errstate(divide="ignore"):
+        e = np.floor(np.log2(np.where(ax > 0, ax, 1.0)))
+    e = np.maximum(e, -6.0)  # below the smallest normal 2**-6 the step is fixed
+    step = np.exp2(e - 3.0)
+    q = np.rint(ax / step) * step  # rint: ties to even
+    q = np.minimum(q, 448.0)
+    return (np.sign(x) * q).astype(np.float32)
+
+
+def quantize_fp8(D):
+    """Per-token e4m3 quantisation (the library's FP8 document format):
+    scale = max|x| / 448 in fp32 (1 for an all-zero token),
+    code = e4m3(x / scale). Returns (e4m3 values as fp32 [B, Ld, d],
+    scales fp32 [B, Ld, 1])."""
+    Df = np.asarray(D).astype(np.float32)
+    amax = np.abs(Df).max(axis=-1, keepdims=True)
+    scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    return e4m3_round(Df / scale), scale
+
+
+def dequantize_fp8(codes_f32, scales) -> np.ndarray:
+    """e4m3 value * scale in fp32."""
+    return np.asarray(codes_f32, dtype=np.float32) * np.asarray(scales, dtype=np.float32)
+
+
 def maxsim_sparse(Q, D, indices, doc_lengths=None) -> np.ndarray:
     """maxsim_sparse_naive (flash_maxsim/flash_maxsim_sparse.py:143-157), plus
     the length mask the sparse kernel applies (:60-80):

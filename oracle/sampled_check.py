@@ -60,6 +60,13 @@ def check_int8(Q, u8_rows, sc_rows, mn_rows, got, lens_rows=None) -> dict:
     return _compare(got, want, "int8 scores")
 
 
+def check_fp8(Q, codes_f32_rows, sc_rows, got, lens_rows=None) -> dict:
+    """FP8 scores of sampled documents against maxsim_naive on the
+    dequantised documents (e4m3 value * per-token scale). Q: [Lq, d]; got: [n]."""
+    want = O.maxsim(Q, O.dequantize_fp8(codes_f32_rows, sc_rows), lens_rows)
+    return _compare(got, want, "fp8 scores")
+
+
 def check_train(Q, D_rows, lens_rows, g_rows, scores_rows, am_rows, dD_rows,
                 dq_rows_idx, dq_got, dq_want_inputs, eps: float = 1e-4) -> dict:
     """Training forward + backward on sampled documents, tie-aware.

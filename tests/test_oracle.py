@@ -80,3 +80,21 @@ def test_argmax_first_occurrence():
     assert am[0, 0] == 1 and s[0] == 1.0 and gap[0, 0] == 0.0
     s, am, _ = O.maxsim_argmax(Q, D, doc_lengths=np.array([1]))
     assert am[0, 0] == 0 and s[0] == 0.5
+
+
+def test_e4m3_rounding_matches_torch():
+    # the oracle's e4m3 rounding (FP8 document format) against torch's own
+    # float8_e4m3fn conversion: random values over many scales, every exact
+    # midpoint between neighbouring codes (ties to even) and every code
+    import torch
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(20000).astype(np.float32) * s for s in (1e-4, 1e-2, 1.0, 50.0)])
+    x = x[np.abs(x) <= 448]
+    grid = torch.arange(0, 256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    grid = np.unique(grid[np.isfinite(grid)])
+    mids = ((grid[1:] + grid[:-1]) / 2).astype(np.float32)
+    x = np.concatenate([x, mids, -mids, grid, -grid])
+    want = torch.from_numpy(x).to(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(O.e4m3_round(x), want)
+    # values past the largest code saturate (torch would give NaN there)
+    np.testing.assert_array_equal(O.e4m3_round(np.array([460.0, -1e4], np.float32)), [448.0, -448.0])
