@@ -44,6 +44,8 @@ SIGNATURES = {
     "fm_maxsim_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "fm_maxsim_fp8_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "fm_quantize_fp8": (_I, [_P, _I, _P, _P, _I64, _I, _P]),
+    "fm_normalize_quantize_int8": (_I, [_P, _I, _P, _P, _P, _I64, _I, _P]),
+    "fm_normalize_quantize_fp8": (_I, [_P, _I, _P, _P, _I64, _I, _P]),
     "fm_quantize_int8": (_I, [_P, _I, _P, _P, _P, _I64, _I, _P]),
     "fm_wait_selftest": (_I, [_P, _I64, _P]),
     "fm_fwd_plan_info": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I]),

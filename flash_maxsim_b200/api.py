@@ -399,19 +399,24 @@ _QDTYPE = {torch.float16: _lib.FM_DTYPE_F16, torch.float32: _lib.FM_DTYPE_F32,
            torch.bfloat16: _lib.FM_DTYPE_BF16}
 
 
-def quantize_int8(D: torch.Tensor):
+def quantize_int8(D: torch.Tensor, normalize: bool = False):
     """Per-token affine INT8 quantisation (flash_maxsim/flash_maxsim_quant.py:11-28).
 
     D: [B, Ld, d] -> (uint8 [B, Ld, d], scales fp16 [B, Ld, 1], mins fp16 [B, Ld, 1]),
     bit-identical to the reference formula, computed by one CUDA kernel pass.
+    normalize=True (index time): every token row is first L2-normalised in the
+    same pass (see normalize_quantize_int8).
     """
     assert D.dim() == 3
     _require_cuda(D)
+    fn = lib.fm_normalize_quantize_int8 if normalize else lib.fm_quantize_int8
     B, Ld, d = D.shape
     x = D if D.dtype in _QDTYPE else D.float()
     # the kernel reads 8 elements per lane: pad rows with their own first
     # element (changes neither min nor max), then drop the padded columns
     pad = (-d) % 8
+    if pad and normalize:
+        raise ValueError(f"normalize=True needs d % 8 == 0 (got d={d})")
     if pad:
         x = torch.cat([x, x[..., :1].expand(B, Ld, pad)], dim=-1)
     x = _aligned(x)
@@ -423,10 +428,9 @@ def quantize_int8(D: torch.Tensor):
     if rows:
         _before_call(D.device)
         with _lib.on_device(D.device):
-            rc = lib.fm_quantize_int8(x.data_ptr(), _QDTYPE[x.dtype], u8.data_ptr(),
-                                      scales.data_ptr(), mins.data_ptr(), rows, dp,
-                                      _lib.stream_of(D.device))
-        _lib.check(rc, "fm_quantize_int8")
+            rc = fn(x.data_ptr(), _QDTYPE[x.dtype], u8.data_ptr(), scales.data_ptr(), mins.data_ptr(), rows, dp,
+                    _lib.stream_of(D.device))
+        _lib.check(rc, "fm_normalize_quantize_int8" if normalize else "fm_quantize_int8")
         _after_call(D.device)
     if pad:
         u8 = u8[..., :d].contiguous()
@@ -482,18 +486,20 @@ def flash_maxsim_int8(Q: torch.Tensor, D_uint8: torch.Tensor, scales: torch.Tens
 # FP8 (e4m3) document storage: the INT8 path's sibling with one scale per token
 # ---------------------------------------------------------------------------
 
-def quantize_fp8(D: torch.Tensor):
+def quantize_fp8(D: torch.Tensor, normalize: bool = False):
     """Per-token e4m3 quantisation on the GPU: D [B, Ld, d] (fp16 / bf16 /
     fp32) -> (codes uint8 [B, Ld, d] holding e4m3 bit patterns, scales fp32
     [B, Ld, 1]) with scale = max|x| / 448 (1 for an all-zero token) and
-    code = e4m3(x / scale), round-to-nearest-even."""
+    code = e4m3(x / scale), round-to-nearest-even. normalize=True (index
+    time): every token row is first L2-normalised in the same pass."""
     assert D.dim() == 3
     _require_cuda(D)
+    fn = lib.fm_normalize_quantize_fp8 if normalize else lib.fm_quantize_fp8
     B, Ld, d = D.shape
     x = D if D.dtype in _QDTYPE else D.float()
     pad = (-d) % 8
     if pad:
-        x = F.pad(x, (0, pad))  # zeros change no row's max |x|
+        x = F.pad(x, (0, pad))  # zeros change no row's max |x| and no norm
     x = _aligned(x)
     dp = d + pad
     codes = torch.empty(B, Ld, dp, device=D.device, dtype=torch.uint8)
@@ -502,9 +508,9 @@ def quantize_fp8(D: torch.Tensor):
     if rows:
         _before_call(D.device)
         with _lib.on_device(D.device):
-            rc = lib.fm_quantize_fp8(x.data_ptr(), _QDTYPE[x.dtype], codes.data_ptr(), scales.data_ptr(), rows, dp,
-                                     _lib.stream_of(D.device))
-        _lib.check(rc, "fm_quantize_fp8")
+            rc = fn(x.data_ptr(), _QDTYPE[x.dtype], codes.data_ptr(), scales.data_ptr(), rows, dp,
+                    _lib.stream_of(D.device))
+        _lib.check(rc, "fm_normalize_quantize_fp8" if normalize else "fm_quantize_fp8")
         _after_call(D.device)
     if pad:
         codes = codes[..., :d].contiguous()

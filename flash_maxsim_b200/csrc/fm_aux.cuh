@@ -256,7 +256,28 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
 // 256-element segment.  T = __half, float or __nv_bfloat16 (the reference
 // widens any input to fp32 before its min/max, so every type is quantised
 // from its own exact fp32 value).
-template <typename T, int LPR, int NR>
+// Index-time normalisation (NORM = true): every row is first divided by
+// max(||x||_2, 1e-12) (F.normalize's rule) with the norm summed in a fixed
+// order -- per lane x*x over its elements in order (no fused multiply-add),
+// then an xor butterfly over the row's lanes -- and an IEEE square root and
+// division, so the result is reproducible bit for bit on the host.
+template <int LPR, int NSEG>
+__device__ __forceinline__ float row_inv_norm_sq(const float (&v)[NSEG][8], int nseg, int l, int d) {
+  float s = 0.f;
+#pragma unroll
+  for (int g = 0; g < NSEG; ++g) {
+    const int k = (g * LPR + l) * 8;
+    if (g < nseg && k < d) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s = __fadd_rn(s, __fmul_rn(v[g][j], v[g][j]));
+    }
+  }
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+  return s;
+}
+
+template <typename T, int LPR, int NR, bool NORM = false>
 __global__ void __launch_bounds__(256) quantize_int8_kernel(const T* __restrict__ D,
                                                             uint8_t* __restrict__ U,
                                                             __half* __restrict__ scales,
@@ -283,6 +304,16 @@ __global__ void __launch_bounds__(256) quantize_int8_kernel(const T* __restrict_
     for (int s = 0; s < SEG; ++s) {
       const int k = (s * LPR + l) * 8;
       if (row < rows && s < nseg && k < d) load8(src + k, v[r][s]);
+    }
+  }
+  if (NORM) {
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const float den = fmaxf(__fsqrt_rn(row_inv_norm_sq<LPR, SEG>(v[r], nseg, l, d)), 1e-12f);
+#pragma unroll
+      for (int s = 0; s < SEG; ++s)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[r][s][j] = __fdiv_rn(v[r][s][j], den);
     }
   }
 #pragma unroll

@@ -880,31 +880,6 @@ int fm_maxsim_fp8_fwd(const uint16_t* Q, const uint8_t* D_fp8, const float* scal
                     nullptr);
 }
 
-int fm_quantize_fp8(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d, void* stream) {
-  if (!D || !D_fp8 || !scales || rows < 0 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
-  if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_fp8) & 7u)) return FM_ERR_ARG;
-  if (rows == 0) return FM_OK;
-  const int64_t blocks = (rows + 7) / 8;
-  if (blocks > INT32_MAX) return FM_ERR_ARG;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned nb = static_cast<unsigned>(blocks);
-  switch (dtype) {
-    case FM_DTYPE_F16:
-      quantize_fp8_kernel<__half><<<nb, 256, 0, st>>>(static_cast<const __half*>(D), D_fp8, scales, rows, d);
-      break;
-    case FM_DTYPE_F32:
-      quantize_fp8_kernel<float><<<nb, 256, 0, st>>>(static_cast<const float*>(D), D_fp8, scales, rows, d);
-      break;
-    case FM_DTYPE_BF16:
-      quantize_fp8_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(D), D_fp8, scales,
-                                                               rows, d);
-      break;
-    default:
-      return FM_ERR_ARG;
-  }
-  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
-}
-
 int64_t fm_topk_workspace_size(int Nq, int k) {
   if (Nq < 1 || k < 1 || k > kTopkMaxK) return 0;
   const int64_t b = topk_ws_bytes(Nq, k);
@@ -1080,8 +1055,13 @@ int fm_maxsim_bwd_noalloc(const uint16_t* Q, const uint16_t* D, const int32_t* a
                   static_cast<int64_t>(kNoAllocScratchBytes), static_cast<cudaStream_t>(stream));
 }
 
-int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,
-                     int64_t rows, int d, void* stream) {
+}  // extern "C"
+
+namespace fm {
+namespace {
+template <bool NORM>
+int quantize_int8_impl(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins, int64_t rows,
+                       int d, void* stream) {
   if (!D || !D_u8 || !scales || !mins || rows < 0 || d < 8 || d > 2048 || d % 8 != 0)
     return FM_ERR_ARG;
   if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_u8) & 7u)) return FM_ERR_ARG;
@@ -1100,10 +1080,10 @@ int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, 
   auto launch = [&](auto tag) {
     using T = decltype(tag);
     const T* src = static_cast<const T*>(D);
-    if (lpr == 8) quantize_int8_kernel<T, 8, 4><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
-    else if (lpr == 16) quantize_int8_kernel<T, 16, 4><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
-    else if (nr == 4) quantize_int8_kernel<T, 32, 4><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
-    else quantize_int8_kernel<T, 32, 1><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    if (lpr == 8) quantize_int8_kernel<T, 8, 4, NORM><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    else if (lpr == 16) quantize_int8_kernel<T, 16, 4, NORM><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    else if (nr == 4) quantize_int8_kernel<T, 32, 4, NORM><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
+    else quantize_int8_kernel<T, 32, 1, NORM><<<nb, 256, 0, st>>>(src, D_u8, sc, mn, rows, d);
   };
   switch (dtype) {
     case FM_DTYPE_F16: launch(__half{}); break;
@@ -1113,6 +1093,55 @@ int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, 
       return FM_ERR_ARG;
   }
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+
+template <bool NORM>
+int quantize_fp8_impl(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d, void* stream) {
+  if (!D || !D_fp8 || !scales || rows < 0 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
+  if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_fp8) & 7u)) return FM_ERR_ARG;
+  if (rows == 0) return FM_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > INT32_MAX) return FM_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned nb = static_cast<unsigned>(blocks);
+  switch (dtype) {
+    case FM_DTYPE_F16:
+      quantize_fp8_kernel<__half, NORM><<<nb, 256, 0, st>>>(static_cast<const __half*>(D), D_fp8, scales, rows, d);
+      break;
+    case FM_DTYPE_F32:
+      quantize_fp8_kernel<float, NORM><<<nb, 256, 0, st>>>(static_cast<const float*>(D), D_fp8, scales, rows, d);
+      break;
+    case FM_DTYPE_BF16:
+      quantize_fp8_kernel<__nv_bfloat16, NORM><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(D), D_fp8,
+                                                                     scales, rows, d);
+      break;
+    default:
+      return FM_ERR_ARG;
+  }
+  return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
+}
+}  // namespace
+}  // namespace fm
+
+extern "C" {
+
+int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins, int64_t rows,
+                     int d, void* stream) {
+  return quantize_int8_impl<false>(D, dtype, D_u8, scales, mins, rows, d, stream);
+}
+
+int fm_normalize_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,
+                               int64_t rows, int d, void* stream) {
+  return quantize_int8_impl<true>(D, dtype, D_u8, scales, mins, rows, d, stream);
+}
+
+int fm_quantize_fp8(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d, void* stream) {
+  return quantize_fp8_impl<false>(D, dtype, D_fp8, scales, rows, d, stream);
+}
+
+int fm_normalize_quantize_fp8(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d,
+                              void* stream) {
+  return quantize_fp8_impl<true>(D, dtype, D_fp8, scales, rows, d, stream);
 }
 
 #ifdef FM_PROFILE

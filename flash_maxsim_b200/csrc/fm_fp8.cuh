@@ -395,19 +395,32 @@ __global__ void __launch_bounds__(f8_threads(), 1)
 // token), code = e4m3(x / scale) with round-to-nearest-even and saturation
 // (|x / scale| <= 448 up to rounding).  One warp per token row, 8 elements
 // per lane; T = __half, float or __nv_bfloat16.
-template <typename T>
+// With NORM, every row is first divided by max(||x||_2, 1e-12), the norm
+// summed in the fixed order of row_inv_norm_sq (32 lanes per row).
+template <typename T, bool NORM = false>
 __global__ void __launch_bounds__(256) quantize_fp8_kernel(const T* __restrict__ D, uint8_t* __restrict__ codes,
                                                            float* __restrict__ scales, int64_t rows, int d) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const T* src = D + row * d;
+  float den = 1.f;
+  if (NORM) {
+    float v[kMaxSeg][8];
+    const int nseg = (d + 255) / 256;
+#pragma unroll
+    for (int g = 0; g < kMaxSeg; ++g) {
+      const int k = (g * 32 + lane) * 8;
+      if (g < nseg && k < d) load8(src + k, v[g]);
+    }
+    den = fmaxf(__fsqrt_rn(row_inv_norm_sq<32, kMaxSeg>(v, nseg, lane, d)), 1e-12f);
+  }
   float amax = 0.f;
   for (int k = lane * 8; k < d; k += 256) {
     float f[8];
     load8(src + k, f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(NORM ? __fdiv_rn(f[j], den) : f[j]));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -418,7 +431,7 @@ __global__ void __launch_bounds__(256) quantize_fp8_kernel(const T* __restrict__
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint32_t c = e4m3_bits(__fdiv_rn(f[j], scale));
+      const uint32_t c = e4m3_bits(__fdiv_rn(NORM ? __fdiv_rn(f[j], den) : f[j], scale));
       if (j < 4) w0 |= c << (8 * j);
       else w1 |= c << (8 * (j - 4));
     }

@@ -245,6 +245,21 @@ int fm_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, 
                      int64_t rows, int d, void* stream);
 
 /*
+ * Index-time quantisation of freshly encoded embeddings, fused with their
+ * L2 normalisation: every row is divided by max(||x||_2, 1e-12) (the rule of
+ * torch.nn.functional.normalize, the norm summed in a fixed order so that the
+ * result is reproducible on the host) and then quantised exactly as
+ * fm_quantize_int8 / fm_quantize_fp8 quantise their input. One pass over the
+ * embeddings instead of a normalise pass, a cast and a quantise pass. No
+ * counterpart in the reference (its quantize_int8 takes normalised input,
+ * flash_maxsim/flash_maxsim_quant.py:11-28).
+ */
+int fm_normalize_quantize_int8(const void* D, int dtype, uint8_t* D_u8, uint16_t* scales, uint16_t* mins,
+                               int64_t rows, int d, void* stream);
+int fm_normalize_quantize_fp8(const void* D, int dtype, uint8_t* D_fp8, float* scales, int64_t rows, int d,
+                              void* stream);
+
+/*
  * Failure-detection self test: launches one CTA that waits on a barrier that
  * nothing arrives at. The bounded wait gives up after timeout_ns and writes
  * FM_ERR_TIMEOUT_SELFTEST into *status; the context stays usable.

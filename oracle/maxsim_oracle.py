@@ -136,6 +136,51 @@ def dequantize_int8(u8, scales, mins) -> np.ndarray:
             + np.asarray(mins).astype(np.float32))
 
 
+def l2_normalize_rows(x) -> np.ndarray:
+    """Rows divided by max(||x||_2, 1e-12) (torch.nn.functional.normalize's
+    rule) with the norm summed in the library's fixed order: lane
+    l = 0..LPR-1 of a row sums x*x over its elements k = (s * LPR + l) * 8 + j
+    (s, then j ascending; fp32, rounded after every operation), then the
+    lanes are combined by an xor butterfly (offsets LPR/2, ..., 1); LPR = 8
+    for d <= 64, 16 for d <= 128, else 32 (the FP8 kernel always uses 32)."""
+    x = np.asarray(x, dtype=np.float32)
+    d = x.shape[-1]
+    return _l2_normalize_rows(x, 8 if d <= 64 else (16 if d <= 128 else 32))
+
+
+def _l2_normalize_rows(x, lpr: int) -> np.ndarray:
+    d = x.shape[-1]
+    flat = x.reshape(-1, d)
+    lanes = []
+    for l in range(lpr):
+        acc = np.zeros(flat.shape[0], dtype=np.float32)
+        s = 0
+        while (s * lpr + l) * 8 < d:
+            for j in range(8):
+                k = (s * lpr + l) * 8 + j
+                if k < d:
+                    acc = (acc + (flat[:, k] * flat[:, k]).astype(np.float32)).astype(np.float32)
+            s += 1
+        lanes.append(acc)
+    o = lpr // 2
+    while o > 0:
+        lanes = [(lanes[i] + lanes[i ^ o]).astype(np.float32) for i in range(lpr)]
+        o //= 2
+    den = np.maximum(np.sqrt(lanes[0]).astype(np.float32), np.float32(1e-12))
+    return (flat / den[:, None]).astype(np.float32).reshape(x.shape)
+
+
+def normalize_quantize_int8(D):
+    """Index-time INT8: quantize_int8 of the L2-normalised rows."""
+    return quantize_int8(l2_normalize_rows(D))
+
+
+def normalize_quantize_fp8(D):
+    """Index-time FP8: quantize_fp8 of the L2-normalised rows (32-lane order)."""
+    x = np.asarray(D, dtype=np.float32)
+    return quantize_fp8(_l2_normalize_rows(x, 32))
+
+
 def e4m3_round(x) -> np.ndarray:
     """Round fp32 values to the nearest e4m3 (fn variant: 4 exponent bits,
     bias 7, 3 mantissa bits, subnormal step 2**-9, largest finite 448, no
