@@ -225,6 +225,132 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd_kernel(
   }
 }
 
+// dD, one CTA per document, every warp busy in every phase.  The (query,
+// row) entries e that picked a token of this document are bucketed by token
+// with a stable counting sort: warp w counts the tokens of its slice of
+// entries (slices in entry order), the counts become offsets in (token,
+// warp) order, and each warp scatters its slice in order -- so every bucket
+// lists its entries in ascending e, the same fixed summation order as the
+// single-warp sort.  Then each warp owns tokens t = w, w + 8, ...: it adds
+// g[n] * Q[e] over the bucket with four query-row gathers in flight and
+// writes the whole token row (zeros for untouched tokens).
+// Shared memory: cnt[8][Ld + 1] + base[Ld + 2] + order[Nq * Lq] ints, g[Nq].
+constexpr int kDdWarps = kBwdThreads / 32;
+__host__ __device__ constexpr size_t dd2_smem_bytes(int Nq, int Lq, int Ld) {
+  return (static_cast<size_t>(kDdWarps) * (Ld + 1) + (Ld + 2) + static_cast<size_t>(Nq) * Lq) * 4 +
+         static_cast<size_t>(Nq) * 4;
+}
+
+__global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd2_kernel(
+    const __half* __restrict__ Q, const int32_t* __restrict__ am, const float* __restrict__ g,
+    __half* __restrict__ dD, int Nq, int B, int Lq, int Ld, int d) {
+  extern __shared__ int sm_i[];
+  const int b = blockIdx.x;
+  const int E = Nq * Lq;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  int* cnt = sm_i;                                  // [kDdWarps][Ld + 1]
+  int* base = cnt + kDdWarps * (Ld + 1);            // [Ld + 2]
+  int* order = base + (Ld + 2);                     // [E]
+  float* gs = reinterpret_cast<float*>(order + E);  // [Nq]
+
+  for (int i = tid; i < kDdWarps * (Ld + 1); i += kBwdThreads) cnt[i] = 0;
+  for (int n = tid; n < Nq; n += kBwdThreads) gs[n] = __ldg(g + static_cast<size_t>(n) * B + b);
+  __syncthreads();
+  auto entry_tok = [&](int e) -> int {
+    const int n = e / Lq, q = e - n * Lq;
+    const int t = __ldg(am + (static_cast<size_t>(n) * B + b) * Lq + q);
+    return (t >= 0 && t < Ld) ? t : -1;
+  };
+  const int e_lo = static_cast<int>(static_cast<int64_t>(E) * warp / kDdWarps);
+  const int e_hi = static_cast<int>(static_cast<int64_t>(E) * (warp + 1) / kDdWarps);
+  int* mycnt = cnt + warp * (Ld + 1);
+  for (int e = e_lo + lane; e < e_hi; e += 32) {
+    const int t = entry_tok(e);
+    if (t >= 0) atomicAdd(&mycnt[t], 1);
+  }
+  __syncthreads();
+  // per token: offsets of the warps' runs inside the token's bucket; the
+  // bucket sizes go to base[t]
+  for (int t = tid; t < Ld; t += kBwdThreads) {
+    int run = 0;
+#pragma unroll
+    for (int w = 0; w < kDdWarps; ++w) {
+      const int c = cnt[w * (Ld + 1) + t];
+      cnt[w * (Ld + 1) + t] = run;
+      run += c;
+    }
+    base[t] = run;
+  }
+  __syncthreads();
+  // exclusive scan of base[0..Ld) into base[0..Ld] (warp 0, contiguous lane ranges)
+  if (warp == 0) {
+    const int per = (Ld + 31) / 32;
+    const int lo = lane * per, hi = min(Ld, lo + per);
+    int s = 0;
+    for (int t = lo; t < hi; ++t) s += base[t];
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - s;
+    for (int t = lo; t < hi; ++t) {
+      const int c = base[t];
+      base[t] = run;
+      run += c;
+    }
+    if (lane == 31) base[Ld] = incl;
+  }
+  __syncthreads();
+  // stable scatter of each warp's slice, in entry order
+  for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
+    const int e = e0 + lane;
+    const int t = (e < e_hi) ? entry_tok(e) : -1;
+    const unsigned grp = __match_any_sync(0xffffffffu, t);
+    if (t >= 0) {
+      const int rank = __popc(grp & ((1u << lane) - 1u));
+      order[base[t] + mycnt[t] + rank] = e;
+    }
+    __syncwarp();
+    if (t >= 0 && lane == __ffs(grp) - 1) mycnt[t] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  const int nseg = (d + 255) / 256;
+  for (int t = warp; t < Ld; t += kDdWarps) {
+    const int beg = base[t], end = base[t + 1];
+    __half* out = dD + (static_cast<size_t>(b) * Ld + t) * d;
+    for (int s = 0; s < nseg; ++s) {
+      const int k = s * 256 + lane * 8;
+      const bool kin = k < d;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      int p = beg;
+      for (; p + 4 <= end; p += 4) {
+        uint4 raw[4];
+        float gv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = order[p + u];
+          gv[u] = gs[e / Lq];
+          raw[u] = kin ? __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k))
+                       : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) fma8(acc, raw[u], gv[u]);
+      }
+      for (; p < end; ++p) {
+        const int e = order[p];
+        if (kin) fma8(acc, __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k)), gs[e / Lq]);
+      }
+      if (kin) *reinterpret_cast<uint4*>(out + k) = pack8(acc);
+    }
+  }
+}
+
 // 8 consecutive elements of a row as fp32 (exact widening)
 __device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
   const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));

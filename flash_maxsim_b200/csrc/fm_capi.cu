@@ -398,7 +398,7 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   if (a.nts % 2) return false;  // the two warps of a lane quarter own alternate slots
   a.atoms = cdiv(d, 128);
   a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
-  a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);
+  a.sc_slot_bytes = 0;  // per-token scales and mins are read by the epilogue threads themselves
   const int q_bytes = a.atoms * a.N * 128;
   const int misc = round_up((64 + 64 + kI8Xch * 8 * gq * 32) * 4 + 2 * kI8Xch * 4, 16);
   const int per_slot = static_cast<int>(a.u_slot_bytes + a.sc_slot_bytes) + 16;
@@ -972,14 +972,25 @@ int bwd_impl(const uint16_t* Q, const uint16_t* D, const int32_t* argmax, const 
   static std::atomic<bool> dd_cfg{false};
   if (!dd_cfg.load()) {
     if (cudaFuncSetAttribute(maxsim_bwd_dd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(maxsim_bwd_dd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxSmem) != cudaSuccess)
       return FM_ERR_LAUNCH;
     dd_cfg.store(true);
   }
-  if (!(tune().dbg & 16))
-    maxsim_bwd_dd_kernel<<<B, kBwdThreads, smem, st>>>(
-        reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D), Nq,
-        B, Lq, Ld, d);
+  // every warp sorts and scatters (per-warp counts) when they fit in shared
+  // memory; otherwise the single-sorter kernel (same summation order)
+  const size_t smem2 = dd2_smem_bytes(Nq, Lq, Ld);
+  if (!(tune().dbg & 16)) {
+    if (smem2 <= static_cast<size_t>(kMaxSmem))
+      maxsim_bwd_dd2_kernel<<<B, kBwdThreads, smem2, st>>>(
+          reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D), Nq, B, Lq,
+          Ld, d);
+    else
+      maxsim_bwd_dd_kernel<<<B, kBwdThreads, smem, st>>>(
+          reinterpret_cast<const __half*>(Q), argmax, grad_scores, reinterpret_cast<__half*>(grad_D), Nq, B, Lq,
+          Ld, d);
+  }
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 

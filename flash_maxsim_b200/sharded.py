@@ -137,3 +137,36 @@ def sharded_maxsim_batched(Q: torch.Tensor, D_local: torch.Tensor, B: int, doc_l
         return topk_merge_candidates(cand_v, cand_i, k)
     local = flash_maxsim_batched(Q, D_local, doc_lengths_local)
     return all_gather_scores(local, B, group)
+
+
+class _SumGradAcrossRanks(torch.autograd.Function):
+    """Identity forward; the backward all-reduces (sums) the gradient over the
+    group, so a query shared by every rank receives the gradient of the
+    scores of all shards."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, grad):
+        grad = grad.contiguous()
+        dist.all_reduce(grad, op=dist.ReduceOp.SUM, group=ctx.group)
+        return grad, None
+
+
+def sum_grad_across_ranks(x: torch.Tensor, group=None) -> torch.Tensor:
+    return _SumGradAcrossRanks.apply(x, group)
+
+
+def sharded_maxsim_train(Q: torch.Tensor, D_local: torch.Tensor, doc_lengths_local=None, group=None):
+    """Doc-sharded training forward: this rank's scores [Nq, B_rank] (or
+    [B_rank] for Q [Lq, d]) of its document shard, with autograd. The
+    backward gives dD for the local documents and dQ summed over all ranks
+    (one NCCL all-reduce of Nq * Lq * d values), so every rank holds the same
+    query gradient as a single-GPU run over the whole corpus (up to the
+    order of the fp32 sums). The caller's loss must be computed on the local
+    scores (or on scores gathered with torch.distributed.nn)."""
+    from .api import flash_maxsim_train
+    return flash_maxsim_train(sum_grad_across_ranks(Q, group), D_local, doc_lengths_local)

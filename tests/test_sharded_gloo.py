@@ -97,3 +97,33 @@ def test_failed_rank_is_detected_not_hung():
         p.join(timeout=60)
     assert res[1] == "raised"
     assert res[0].startswith("error:")
+
+
+def _grad_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from flash_maxsim_b200 import sharded
+        x = torch.arange(6, dtype=torch.float32).reshape(2, 3).requires_grad_(True)
+        y = sharded.sum_grad_across_ranks(x)
+        (y * (rank + 1)).sum().backward()
+        q.put((rank, x.grad.clone()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_query_gradient_summed_over_ranks():
+    # the doc-sharded training path sums dQ over ranks: rank r contributes r + 1
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_grad_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for _, g in res:
+        assert torch.equal(g, torch.full((2, 3), 3.0))
