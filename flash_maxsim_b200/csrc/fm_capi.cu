@@ -398,7 +398,7 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   if (a.nts % 2) return false;  // the two warps of a lane quarter own alternate slots
   a.atoms = cdiv(d, 128);
   a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
-  a.sc_slot_bytes = 0;  // per-token scales and mins are read by the epilogue threads themselves
+  a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);
   const int q_bytes = a.atoms * a.N * 128;
   const int misc = round_up((64 + 64 + kI8Xch * 8 * gq * 32) * 4 + 2 * kI8Xch * 4, 16);
   const int per_slot = static_cast<int>(a.u_slot_bytes + a.sc_slot_bytes) + 16;

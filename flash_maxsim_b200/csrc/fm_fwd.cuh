@@ -226,31 +226,12 @@ struct RowAcc {
 template <bool ARGMAX>
 __device__ __forceinline__ void piece_max(const float (&v)[32], int nv, int col0, RowAcc<ARGMAX>& acc) {
   if (ARGMAX) {
-    // pairwise tree (depth 5 instead of a 32-long dependency chain); at equal
-    // values the lower column wins, so the first occurrence is kept
-    float m[16];
-    int ix[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float a0 = (2 * i < nv) ? v[2 * i] : -INFINITY;
-      const float a1 = (2 * i + 1 < nv) ? v[2 * i + 1] : -INFINITY;
-      const bool hi = a1 > a0;
-      m[i] = hi ? a1 : a0;
-      ix[i] = hi ? 2 * i + 1 : 2 * i;
-    }
-#pragma unroll
-    for (int st = 1; st < 16; st <<= 1) {
-#pragma unroll
-      for (int i = 0; i < 16; i += 2 * st) {
-        // entry i covers columns just before those of entry i + st
-        const bool hi = m[i + st] > m[i];
-        ix[i] = hi ? ix[i + st] : ix[i];
-        m[i] = hi ? m[i + st] : m[i];
+    for (int i = 0; i < 32; ++i) {
+      if (i < nv && v[i] > acc.m) {
+        acc.m = v[i];
+        acc.idx = col0 + i;
       }
-    }
-    if (m[0] > acc.m) {  // this piece lies after every column seen so far
-      acc.m = m[0];
-      acc.idx = col0 + ix[0];
     }
   } else {
     if (nv == 32) {

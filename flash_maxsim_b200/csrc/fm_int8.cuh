@@ -21,10 +21,8 @@
 //      S[t, q] = scale_t * alpha_q * (256 <h,u> + <l,u>) / 256 + min_t * sum_k Q[q, k]
 //    (256 <h,u> + <l,u> is an exact integer), masks tokens past the document,
 //    and a 31-shuffle butterfly leaves lane j with the max over the warp's
-//    32 tokens for query row j.  Each thread loads its tokens' scale and
-//    min itself (coalesced 64-byte runs per warp), issued before it waits
-//    for the accumulator, so the producer issues nothing but the TMA box.
-//    The warps' maxima are combined per document.
+//    32 tokens for query row j.  Per-token scale/min arrive by bulk copy
+//    with the chunk.  The four warps' maxima are combined per document.
 //
 // Warp roles: 0 = producer (TMA + bulk copies), 1 = MMA issuer + TMEM owner,
 // 2..5 = epilogue (also build the split query).
@@ -64,7 +62,7 @@ struct Int8Args {
   int nu;                  // uint8 ring slots
   int nts;                 // TMEM slots (two halves of N columns each)
   size_t sc_total_bytes;   // bytes of the scales tensor (B * Ld * 2)
-  uint32_t sc_slot_bytes;  // shared-memory staging of scales / mins per slot (unused: 0)
+  uint32_t sc_slot_bytes;  // fp16 scale span + min span of one chunk
   uint32_t off_q, off_u, off_sc, off_misc, off_bar, u_slot_bytes;
   int dbg;  // tuning builds (FM_TUNING) only: bits that switch off parts of the work
 };
@@ -174,13 +172,38 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
             ok = false;
             break;
           }
-          // the uint8 tile by TMA (each epilogue thread loads its own token's
-          // scale and min from global memory)
-          mbar_expect_tx(u_full(ur.idx), tx);
+          // uint8 tile by TMA; the chunk's fp16 scales and mins by two bulk copies
+          // of the enclosing 16-byte-aligned spans (staging: [scales span][mins span])
+          const size_t e0 = static_cast<size_t>(b) * a.Ld + static_cast<size_t>(c) * kI8Tokens;
+          const size_t byte0 = e0 * 2;
+          const size_t lo16 = byte0 & ~static_cast<size_t>(15);
+          const uint32_t span =
+              static_cast<uint32_t>((byte0 + kI8Tokens * 2 - lo16 + 15) & ~static_cast<size_t>(15));
+          const bool bulk_ok = lo16 + span <= a.sc_total_bytes && !FM_DBG(a, 4);
+          uint8_t* stage = smem + a.off_sc + ur.idx * a.sc_slot_bytes;
+          if (!bulk_ok && !FM_DBG(a, 4)) {
+            // the span would run past the end of the tensors: plain loads (last chunk)
+            __half* ss = reinterpret_cast<__half*>(stage);
+            __half* ms = reinterpret_cast<__half*>(stage + a.sc_slot_bytes / 2);
+            const int sh = static_cast<int>((byte0 - lo16) / 2);
+            const size_t total = static_cast<size_t>(a.B) * a.Ld;
+            for (int t = 0; t < kI8Tokens && e0 + t < total; ++t) {
+              ss[sh + t] = a.scales[e0 + t];
+              ms[sh + t] = a.mins[e0 + t];
+            }
+          }
+          // this arrival also releases the plain stores above
+          mbar_expect_tx(u_full(ur.idx), tx + (bulk_ok ? 2 * span : 0u));
           const uint32_t dst = sbase + a.off_u + ur.idx * a.u_slot_bytes;
           for (int at = 0; at < a.atoms; ++at)
             tma_load_3d(dst + at * kI8Tokens * 128, &tmap_u, at * 128, c * kI8Tokens, b, u_full(ur.idx),
                         pol);
+          if (bulk_ok) {
+            const uint32_t st = smem_u32(stage);
+            bulk_load(st, reinterpret_cast<const uint8_t*>(a.scales) + lo16, span, u_full(ur.idx), pol);
+            bulk_load(st + a.sc_slot_bytes / 2, reinterpret_cast<const uint8_t*>(a.mins) + lo16, span,
+                      u_full(ur.idx), pol);
+          }
           ur.next(a.nu);
           ++issued;
         }
@@ -334,31 +357,25 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
           ur.next(a.nu);
           continue;
         }
-        // this thread's tokens' scales and mins, loaded before the waits
-        const bool full = (c + 1) * kI8Tokens <= len;  // whole chunk valid (warp-uniform)
-        float s_tok[kI8Halves], m_tok[kI8Halves];
-        {
-          const size_t e0 = static_cast<size_t>(b) * a.Ld + static_cast<size_t>(c) * kI8Tokens;
-#pragma unroll
-          for (int hb = 0; hb < kI8Halves; ++hb) {
-            const int tic = hb * kI8Half + tok_in_chunk;
-            const bool v = c * kI8Tokens + tic < len;
-            s_tok[hb] = v ? __half2float(__ldg(a.scales + e0 + tic)) : 0.f;
-            m_tok[hb] = v ? __half2float(__ldg(a.mins + e0 + tic)) : 0.f;
-          }
-        }
+        // u_full also publishes the chunk's scales/mins; the slot is not refilled
+        // before this warp releases it below
         if (!mbar_wait(u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
         if (!mbar_wait(t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) { ok = false; break; }
         tc_fence_after();
         FM_PROF_T0(pe0);
+        const size_t byte0 = (static_cast<size_t>(b) * a.Ld + static_cast<size_t>(c) * kI8Tokens) * 2;
+        const uint8_t* stage = smem + a.off_sc + ur.idx * a.sc_slot_bytes;
+        const bool full = (c + 1) * kI8Tokens <= len;  // whole chunk valid (warp-uniform)
 #pragma unroll
         for (int hb = 0; hb < kI8Halves; ++hb) {
           const int tic = hb * kI8Half + tok_in_chunk;
           const bool valid = c * kI8Tokens + tic < len;
           if (!full && !__any_sync(0xffffffffu, valid)) continue;
           const uint32_t th = tmem_base + lane_base + tr.idx * kI8Halves * a.N + hb * a.N;
-          const float m_t = m_tok[hb];
-          const float sa = s_tok[hb] * a256;
+          const int sh = static_cast<int>((byte0 & 15) >> 1) + tic;
+          const float s_t = __half2float(reinterpret_cast<const __half*>(stage)[sh]);
+          const float m_t = __half2float(reinterpret_cast<const __half*>(stage + a.sc_slot_bytes / 2)[sh]);
+          const float sa = s_t * a256;
 #pragma unroll
           for (int g = 0; g < GQ; ++g) {
             uint32_t h[32], l[32];
