@@ -45,8 +45,8 @@ __device__ __forceinline__ uint4 pack8(const float (&acc)[8]) {
 
 // dQ partial sums: grid (ceil(Nq * Lq / 8) row tiles, nsplit document ranges);
 // warp = one query row (n, q), lanes span d (8 fp16 per lane per 256-element
-// segment).  Documents of the range are visited in order, four gathers in
-// flight.  With nsplit == 1 the row is written as fp16 directly; otherwise
+// segment).  Documents of the range are visited in order, eight gathers in
+// flight (four for d > 512).  With nsplit == 1 the row is written as fp16 directly; otherwise
 // the fp32 partial goes to ws[split][row][d] and maxsim_bwd_dq_reduce adds
 // the splits in order.  blockIdx.x (row tiles) varies fastest, so the CTAs
 // that run together read the same document range (L2-resident).
@@ -79,11 +79,12 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dq_kernel(
       gv = __ldg(g + pair);
     }
     const int nb = min(32, b_hi - b0);
-    for (int i = 0; i < nb; i += 4) {
-      uint4 raw[4][NSEG];
-      float gi[4];
+    constexpr int U = NSEG <= 2 ? 8 : 4;  // gathers in flight per lane
+    for (int i = 0; i < nb; i += U) {
+      uint4 raw[U][NSEG];
+      float gi[U];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < U; ++u) {
         const int ti = __shfl_sync(0xffffffffu, t, (i + u) & 31);
         gi[u] = __shfl_sync(0xffffffffu, gv, (i + u) & 31);
         const bool use = (i + u < nb) && ti >= 0 && ti < Ld;  // out-of-range entries count for nothing
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dq_kernel(
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int s = 0; s < NSEG; ++s)
           if (s < nseg) fma8(acc[s], raw[u][s], gi[u]);
@@ -234,10 +235,11 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd_kernel(
 // single-warp sort.  Then each warp owns tokens t = w, w + 8, ...: it adds
 // g[n] * Q[e] over the bucket with four query-row gathers in flight and
 // writes the whole token row (zeros for untouched tokens).
-// Shared memory: cnt[8][Ld + 1] + base[Ld + 2] + order[Nq * Lq] ints, g[Nq].
+// Shared memory: cnt[8][Ld + 1] + base[Ld + 2] + order[Nq * Lq] ints,
+// g of each sorted entry [Nq * Lq] and g[Nq] floats.
 constexpr int kDdWarps = kBwdThreads / 32;
 __host__ __device__ constexpr size_t dd2_smem_bytes(int Nq, int Lq, int Ld) {
-  return (static_cast<size_t>(kDdWarps) * (Ld + 1) + (Ld + 2) + static_cast<size_t>(Nq) * Lq) * 4 +
+  return (static_cast<size_t>(kDdWarps) * (Ld + 1) + (Ld + 2) + 2 * static_cast<size_t>(Nq) * Lq) * 4 +
          static_cast<size_t>(Nq) * 4;
 }
 
@@ -252,22 +254,35 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd2_kernel(
   int* cnt = sm_i;                                  // [kDdWarps][Ld + 1]
   int* base = cnt + kDdWarps * (Ld + 1);            // [Ld + 2]
   int* order = base + (Ld + 2);                     // [E]
-  float* gs = reinterpret_cast<float*>(order + E);  // [Nq]
+  float* gsort = reinterpret_cast<float*>(order + E);  // [E] g of each sorted entry
+  float* gs = gsort + E;                            // [Nq]
 
   for (int i = tid; i < kDdWarps * (Ld + 1); i += kBwdThreads) cnt[i] = 0;
   for (int n = tid; n < Nq; n += kBwdThreads) gs[n] = __ldg(g + static_cast<size_t>(n) * B + b);
   __syncthreads();
-  auto entry_tok = [&](int e) -> int {
-    const int n = e / Lq, q = e - n * Lq;
+  // entry e = n * Lq + q; lanes walk their entries 32 apart with (n, q)
+  // advanced incrementally (no division per entry)
+  auto entry_tok = [&](int n, int q) -> int {
     const int t = __ldg(am + (static_cast<size_t>(n) * B + b) * Lq + q);
     return (t >= 0 && t < Ld) ? t : -1;
+  };
+  auto advance = [&](int& n, int& q) {
+    q += 32;
+    while (q >= Lq) {
+      q -= Lq;
+      ++n;
+    }
   };
   const int e_lo = static_cast<int>(static_cast<int64_t>(E) * warp / kDdWarps);
   const int e_hi = static_cast<int>(static_cast<int64_t>(E) * (warp + 1) / kDdWarps);
   int* mycnt = cnt + warp * (Ld + 1);
-  for (int e = e_lo + lane; e < e_hi; e += 32) {
-    const int t = entry_tok(e);
-    if (t >= 0) atomicAdd(&mycnt[t], 1);
+  {
+    int n = (e_lo + lane) / Lq, q = e_lo + lane - n * Lq;
+    for (int e = e_lo + lane; e < e_hi; e += 32) {
+      const int t = entry_tok(n, q);
+      if (t >= 0) atomicAdd(&mycnt[t], 1);
+      advance(n, q);
+    }
   }
   __syncthreads();
   // per token: offsets of the warps' runs inside the token's bucket; the
@@ -305,14 +320,17 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd2_kernel(
   }
   __syncthreads();
   // stable scatter of each warp's slice, in entry order
+  int sn = (e_lo + lane) / Lq, sq = e_lo + lane - sn * Lq;
   for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
     const int e = e0 + lane;
-    const int t = (e < e_hi) ? entry_tok(e) : -1;
+    const int t = (e < e_hi) ? entry_tok(sn, sq) : -1;
     const unsigned grp = __match_any_sync(0xffffffffu, t);
     if (t >= 0) {
       const int rank = __popc(grp & ((1u << lane) - 1u));
       order[base[t] + mycnt[t] + rank] = e;
+      gsort[base[t] + mycnt[t] + rank] = gs[sn];
     }
+    advance(sn, sq);
     __syncwarp();
     if (t >= 0 && lane == __ffs(grp) - 1) mycnt[t] += __popc(grp);
     __syncwarp();
@@ -335,7 +353,7 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd2_kernel(
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int e = order[p + u];
-          gv[u] = gs[e / Lq];
+          gv[u] = gsort[p + u];
           raw[u] = kin ? __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k))
                        : make_uint4(0, 0, 0, 0);
         }
@@ -344,7 +362,7 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd2_kernel(
       }
       for (; p < end; ++p) {
         const int e = order[p];
-        if (kin) fma8(acc, __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k)), gs[e / Lq]);
+        if (kin) fma8(acc, __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k)), gsort[p]);
       }
       if (kin) *reinterpret_cast<uint4*>(out + k) = pack8(acc);
     }

@@ -846,7 +846,20 @@ int topk_finish(const float* scores, int Nq, int B, int k, TopkArgs t, int parts
   } else {
     t.parts = parts_done;
   }
-  topk_merge_kernel<<<Nq, kTopkThreads, (W + 1) * k * 8, st>>>(t, top_s, top_i, id_offset);
+  // programmatic dependent launch: the merge kernel's launch overlaps the
+  // tail of the kernel that wrote the candidates; it reads them only after
+  // griddepcontrol.wait (that kernel complete, its writes visible)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(Nq);
+  cfg.blockDim = dim3(kTopkThreads);
+  cfg.dynamicSmemBytes = (W + 1) * k * 8;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, topk_merge_kernel, t, top_s, top_i, id_offset) != cudaSuccess) return FM_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 

@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_partial_kernel(const float*
 __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(TopkArgs t, float* __restrict__ out_s,
                                                                    int64_t* __restrict__ out_i, int64_t id_offset) {
   extern __shared__ __align__(16) uint8_t tk_smem[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the candidates' writer has completed
   const int n = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int W = kTopkThreads / 32;
