@@ -250,3 +250,29 @@ def test_bounded_wait_reports_timeout(cuda):
     # still usable afterwards
     Q, D = O.seeded_inputs(1, (32, 128), (4, 20, 128))
     close(fm.flash_maxsim(dev(Q, cuda), dev(D, cuda)).cpu(), O.maxsim(Q, D))
+
+
+def test_backward_ignores_out_of_range_argmax(cuda):
+    # argmax entries outside [0, Ld) (here Ld and Ld + 7) contribute nothing to
+    # dQ or dD, and are never read: the C entry point takes argmax from callers
+    from flash_maxsim_b200 import _lib
+    Nq, Lq, B, Ld, d = 2, 32, 40, 100, 128
+    Q, D = O.seeded_inputs(31, (Nq, Lq, d), (B, Ld, d))
+    am = np.random.default_rng(5).integers(0, Ld, (Nq, B, Lq)).astype(np.int32)
+    am[0, 3, 5] = Ld
+    am[1, B - 1, 0] = Ld + 7
+    am[1, 7, 9] = -1
+    g = np.random.default_rng(6).standard_normal((Nq, B)).astype(np.float32)
+    dQ = torch.empty(Nq, Lq, d, device=cuda, dtype=torch.float16)
+    dD = torch.empty(B, Ld, d, device=cuda, dtype=torch.float16)
+    q, dd, a, gg = dev(Q, cuda), dev(D, cuda), dev(am, cuda), dev(g, cuda)
+    need = int(_lib.lib.fm_maxsim_bwd_workspace_size(Nq, B, Lq, Ld, d))
+    ws = torch.empty(max(need, 16) // 4, device=cuda, dtype=torch.float32)
+    rc = _lib.lib.fm_maxsim_bwd(q.data_ptr(), dd.data_ptr(), a.data_ptr(), gg.data_ptr(), dQ.data_ptr(),
+                                dD.data_ptr(), Nq, B, Lq, Ld, d, ws.data_ptr(), max(need, 16), _lib.stream_of(cuda))
+    assert rc == 0
+    torch.cuda.synchronize(cuda)
+    am_ok = np.where((am >= 0) & (am < Ld), am, -1)
+    wQ, wD = O.maxsim_grads(Q, D, am_ok, g)
+    np.testing.assert_allclose(dQ.float().cpu().numpy(), wQ, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(dD.float().cpu().numpy(), wD, atol=ATOL, rtol=RTOL)
