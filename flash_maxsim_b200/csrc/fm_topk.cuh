@@ -38,6 +38,16 @@ struct TopkCand {
   int b;  // < 0: no candidate
 };
 
+// Order-preserving map of a (non-NaN) float to a nonzero unsigned key:
+// larger floats give larger keys; -inf maps above 0.
+__device__ __forceinline__ unsigned tk_key(float s) {
+  const unsigned u = __float_as_uint(s == 0.f ? 0.f : s);  // -0 and +0 tie
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float tk_unkey(unsigned k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 // (s, b) comes before (bs, bb) in the output order
 __device__ __forceinline__ bool tk_before(float s, int b, float bs, int bb) {
   return s > bs || (s == bs && b < bb);
@@ -86,16 +96,15 @@ __device__ __forceinline__ void warp_topk(int count, int k, Get get, float* out_
         consider(c.s, c.b);
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      const int ob = __shfl_xor_sync(0xffffffffu, bb, o);
-      if (ob >= 0 && (bb < 0 || tk_before(os, ob, bs, bb))) {
-        bs = os;
-        bb = ob;
-      }
-    }
-    if (bb < 0) break;
+    // warp winner with two single-instruction reductions: the largest score
+    // (as an order-preserving unsigned key; 0 = no candidate), then the
+    // smallest document id among the lanes holding it
+    const unsigned key = bb >= 0 ? tk_key(bs) : 0u;
+    const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+    if (kmax == 0u) break;
+    const unsigned id = (key == kmax) ? static_cast<unsigned>(bb) : 0xffffffffu;
+    bb = static_cast<int>(__reduce_min_sync(0xffffffffu, id));
+    bs = tk_unkey(kmax);
     if (lane == 0) {
       out_s[r] = bs;
       out_b[r] = bb;
