@@ -14,8 +14,10 @@
 //
 // Order: score descending, then document id ascending (ties never depend on
 // the schedule, so the result is deterministic and equals a stable sort).
-// A warp selects by k rounds of "best candidate after the previous pick":
-// no storage beyond the candidates themselves, no atomics.
+// A warp selects in k rounds: when its candidates fit in registers (up to 256)
+// each lane sorts its own, and every round takes the best lane head with two
+// single-instruction warp reductions; larger candidate sets are re-read each
+// round ("best candidate after the previous pick").  No atomics.
 #pragma once
 
 #include <cstdint>
@@ -70,8 +72,50 @@ __device__ __forceinline__ void warp_topk(int count, int k, Get get, float* out_
       TopkCand c{0.f, -1};
       if (p < count) c = get(p);
       rs[i] = c.s;
-      rb[i] = c.b;
+      rb[i] = (c.s == c.s) ? c.b : -1;  // NaN scores are never selected
     }
+    // each lane sorts its candidates best first (odd-even transposition;
+    // empty entries last), then every round takes the best lane head and
+    // only the winning lane moves on: no per-round scan of the registers
+#pragma unroll
+    for (int pass = 0; pass < NR; ++pass) {
+#pragma unroll
+      for (int i = pass & 1; i + 1 < NR; i += 2) {
+        const bool sw = rb[i + 1] >= 0 && (rb[i] < 0 || tk_before(rs[i + 1], rb[i + 1], rs[i], rb[i]));
+        const float ts = rs[i];
+        const int tb = rb[i];
+        rs[i] = sw ? rs[i + 1] : rs[i];
+        rb[i] = sw ? rb[i + 1] : rb[i];
+        rs[i + 1] = sw ? ts : rs[i + 1];
+        rb[i + 1] = sw ? tb : rb[i + 1];
+      }
+    }
+    int r = 0;
+    for (; r < k; ++r) {
+      const unsigned key = rb[0] >= 0 ? tk_key(rs[0]) : 0u;
+      const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+      if (kmax == 0u) break;
+      const unsigned id = (key == kmax) ? static_cast<unsigned>(rb[0]) : 0xffffffffu;
+      const int bmin = static_cast<int>(__reduce_min_sync(0xffffffffu, id));
+      if (lane == 0) {
+        out_s[r] = tk_unkey(kmax);
+        out_b[r] = bmin;
+      }
+      if (key == kmax && rb[0] == bmin) {
+#pragma unroll
+        for (int i = 0; i + 1 < NR; ++i) {
+          rs[i] = rs[i + 1];
+          rb[i] = rb[i + 1];
+        }
+        rb[NR - 1] = -1;
+      }
+    }
+    if (lane == 0)
+      for (; r < k; ++r) {
+        out_s[r] = -INFINITY;
+        out_b[r] = -1;
+      }
+    return;
   }
   float ps = INFINITY;  // previous pick; every candidate comes after (+inf, -1)
   int pb = -1;
