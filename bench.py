@@ -493,7 +493,11 @@ def run_config(args, cfg, rank, world, dev, headline: bool) -> dict:
                    "between steps"},
         "roofline": roof, "kernel_ms": round(kern_avg_ms, 4), "clocks": clocks, "parity": par,
         "e2e": e2e, "cpu_baseline": cpu, "reference_gpu": ref_gpu, "topk": topk,
-        "gpu_launches": args.steps * (3 if kind == "train" else 1),
+        # this library's kernels per step: one scoring launch, or for training
+        # the forward, dQ (+ its range reduction when the documents are split)
+        # and dD
+        "gpu_launches": args.steps * ((3 + (1 if fm._lib.lib.fm_maxsim_bwd_workspace_size(Nq, Bl, Lq, Ld, d) > 0 else 0))
+                                      if kind == "train" else 1),
     }
     del w, graphs, graph_out, out_for_check
     torch.cuda.synchronize(dev)
