@@ -1125,21 +1125,23 @@ int quantize_fp8_impl(const void* D, int dtype, uint8_t* D_fp8, float* scales, i
   if (!D || !D_fp8 || !scales || rows < 0 || d < 8 || d > 2048 || d % 8 != 0) return FM_ERR_ARG;
   if (!aligned16(D) || (reinterpret_cast<uintptr_t>(D_fp8) & 7u)) return FM_ERR_ARG;
   if (rows == 0) return FM_OK;
-  const int64_t blocks = (rows + 7) / 8;
+  const int lpr = d <= 64 ? 8 : (d <= 128 ? 16 : 32);
+  const int64_t rows_per_block = 8 * (32 / lpr);
+  const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (blocks > INT32_MAX) return FM_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned nb = static_cast<unsigned>(blocks);
+  auto launch = [&](auto tag) {
+    using T = decltype(tag);
+    const T* src = static_cast<const T*>(D);
+    if (lpr == 8) quantize_fp8_kernel<T, 8, NORM><<<nb, 256, 0, st>>>(src, D_fp8, scales, rows, d);
+    else if (lpr == 16) quantize_fp8_kernel<T, 16, NORM><<<nb, 256, 0, st>>>(src, D_fp8, scales, rows, d);
+    else quantize_fp8_kernel<T, 32, NORM><<<nb, 256, 0, st>>>(src, D_fp8, scales, rows, d);
+  };
   switch (dtype) {
-    case FM_DTYPE_F16:
-      quantize_fp8_kernel<__half, NORM><<<nb, 256, 0, st>>>(static_cast<const __half*>(D), D_fp8, scales, rows, d);
-      break;
-    case FM_DTYPE_F32:
-      quantize_fp8_kernel<float, NORM><<<nb, 256, 0, st>>>(static_cast<const float*>(D), D_fp8, scales, rows, d);
-      break;
-    case FM_DTYPE_BF16:
-      quantize_fp8_kernel<__nv_bfloat16, NORM><<<nb, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(D), D_fp8,
-                                                                     scales, rows, d);
-      break;
+    case FM_DTYPE_F16: launch(__half{}); break;
+    case FM_DTYPE_F32: launch(float{}); break;
+    case FM_DTYPE_BF16: launch(__nv_bfloat16{}); break;
     default:
       return FM_ERR_ARG;
   }

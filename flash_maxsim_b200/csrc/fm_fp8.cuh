@@ -393,51 +393,63 @@ __global__ void __launch_bounds__(f8_threads(), 1)
 
 // Per-token e4m3 quantisation: scale = max|x| / 448 (1 for an all-zero
 // token), code = e4m3(x / scale) with round-to-nearest-even and saturation
-// (|x / scale| <= 448 up to rounding).  One warp per token row, 8 elements
-// per lane; T = __half, float or __nv_bfloat16.
-// With NORM, every row is first divided by max(||x||_2, 1e-12), the norm
-// summed in the fixed order of row_inv_norm_sq (32 lanes per row).
-template <typename T, bool NORM = false>
+// (|x / scale| <= 448 up to rounding).  A row takes LPR lanes (8 elements
+// each per segment, LPR = 8 / 16 / 32 for d <= 64 / 128 / larger, the INT8
+// quantiser's layout), loaded once into registers.  With NORM every row is
+// first divided by max(||x||_2, 1e-12), the norm summed in the fixed order of
+// row_inv_norm_sq.  T = __half, float or __nv_bfloat16.
+template <typename T, int LPR, bool NORM = false>
 __global__ void __launch_bounds__(256) quantize_fp8_kernel(const T* __restrict__ D, uint8_t* __restrict__ codes,
                                                            float* __restrict__ scales, int64_t rows, int d) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  constexpr int RPW = 32 / LPR;                       // rows per warp
+  constexpr int SEG = LPR == 32 ? kMaxSeg : 1;        // segments per lane (d <= 2048)
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const T* src = D + row * d;
-  float den = 1.f;
-  if (NORM) {
-    float v[kMaxSeg][8];
-    const int nseg = (d + 255) / 256;
+  const int sub = lane / LPR, l = lane % LPR;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * RPW + sub;
+  const bool live = row < rows;
+  const int nseg = (d + LPR * 8 - 1) / (LPR * 8);
+  const T* src = D + (live ? row : 0) * d;
+  float v[SEG][8];
 #pragma unroll
-    for (int g = 0; g < kMaxSeg; ++g) {
-      const int k = (g * 32 + lane) * 8;
-      if (g < nseg && k < d) load8(src + k, v[g]);
-    }
-    den = fmaxf(__fsqrt_rn(row_inv_norm_sq<32, kMaxSeg>(v, nseg, lane, d)), 1e-12f);
+  for (int g = 0; g < SEG; ++g) {
+    const int k = (g * LPR + l) * 8;
+    if (live && g < nseg && k < d) load8(src + k, v[g]);
+  }
+  if (NORM) {
+    const float den = fmaxf(__fsqrt_rn(row_inv_norm_sq<LPR, SEG>(v, nseg, l, d)), 1e-12f);
+#pragma unroll
+    for (int g = 0; g < SEG; ++g)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[g][j] = __fdiv_rn(v[g][j], den);
   }
   float amax = 0.f;
-  for (int k = lane * 8; k < d; k += 256) {
-    float f[8];
-    load8(src + k, f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(NORM ? __fdiv_rn(f[j], den) : f[j]));
-  }
+  for (int g = 0; g < SEG; ++g) {
+    const int k = (g * LPR + l) * 8;
+    if (live && g < nseg && k < d) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float scale = amax > 0.f ? amax / 448.f : 1.f;
-  for (int k = lane * 8; k < d; k += 256) {
-    float f[8];
-    load8(src + k, f);
-    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t c = e4m3_bits(__fdiv_rn(NORM ? __fdiv_rn(f[j], den) : f[j], scale));
-      if (j < 4) w0 |= c << (8 * j);
-      else w1 |= c << (8 * (j - 4));
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[g][j]));
     }
-    *reinterpret_cast<uint2*>(codes + row * d + k) = make_uint2(w0, w1);
   }
-  if (lane == 0) scales[row] = scale;
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (!live) return;
+  const float scale = amax > 0.f ? amax / 448.f : 1.f;
+#pragma unroll
+  for (int g = 0; g < SEG; ++g) {
+    const int k = (g * LPR + l) * 8;
+    if (g < nseg && k < d) {
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t c = e4m3_bits(__fdiv_rn(v[g][j], scale));
+        if (j < 4) w0 |= c << (8 * j);
+        else w1 |= c << (8 * (j - 4));
+      }
+      *reinterpret_cast<uint2*>(codes + row * d + k) = make_uint2(w0, w1);
+    }
+  }
+  if (l == 0) scales[row] = scale;
 }
 
 }  // namespace fm

@@ -142,7 +142,7 @@ def l2_normalize_rows(x) -> np.ndarray:
     l = 0..LPR-1 of a row sums x*x over its elements k = (s * LPR + l) * 8 + j
     (s, then j ascending; fp32, rounded after every operation), then the
     lanes are combined by an xor butterfly (offsets LPR/2, ..., 1); LPR = 8
-    for d <= 64, 16 for d <= 128, else 32 (the FP8 kernel always uses 32)."""
+    for d <= 64, 16 for d <= 128, else 32 (both quantisers)."""
     x = np.asarray(x, dtype=np.float32)
     d = x.shape[-1]
     return _l2_normalize_rows(x, 8 if d <= 64 else (16 if d <= 128 else 32))
@@ -176,9 +176,8 @@ def normalize_quantize_int8(D):
 
 
 def normalize_quantize_fp8(D):
-    """Index-time FP8: quantize_fp8 of the L2-normalised rows (32-lane order)."""
-    x = np.asarray(D, dtype=np.float32)
-    return quantize_fp8(_l2_normalize_rows(x, 32))
+    """Index-time FP8: quantize_fp8 of the L2-normalised rows."""
+    return quantize_fp8(l2_normalize_rows(D))
 
 
 def e4m3_round(x) -> np.ndarray:
