@@ -640,17 +640,19 @@ int launch_flat(const Shape& s, const void* Q, const void* D, float* scores, int
 }
 
 // FP8 path (fm_fp8.cuh): one query of <= 64 rows, e4m3 documents, d <= 256.
-bool plan_fp8(int B, int Lq, int Ld, int d, Fp8Args& a, int& smem) {
+// nh: 128-token halves per chunk (2 for one 32-row query, whose TMEM slots of
+// 2 x 96 columns still come in an even number; 1 for 64-row queries).
+bool plan_fp8(int B, int Lq, int Ld, int d, int nh, Fp8Args& a, int& smem) {
   a.B = B;
   a.Lq = Lq;
   a.Ld = Ld;
   a.d = d;
   const int gq = cdiv(Lq, 32);
   a.N = kF8Parts * 32 * gq;
-  a.nts = (512 / a.N) & ~1;  // even: the two warps of a lane quarter own alternate slots
+  a.nts = (512 / (nh * a.N)) & ~1;  // even: the two warps of a lane quarter own alternate slots
   if (a.nts < 2) return false;
   a.atoms = cdiv(d, 128);
-  a.u_slot_bytes = a.atoms * kF8Tokens * 128u;
+  a.u_slot_bytes = a.atoms * nh * kF8Half * 128u;
   const int q_bytes = round_up(a.atoms * a.N * 128, 1024);
   const int misc = round_up((64 + kF8Xch * kF8EW * gq * 32) * 4 + 2 * kF8Xch * 4, 16);
   const int fixed = 1024 + q_bytes + misc + (2 * 16 + 2 * a.nts + 2) * 8 + 32;
@@ -669,18 +671,18 @@ bool plan_fp8(int B, int Lq, int Ld, int d, Fp8Args& a, int& smem) {
   return smem <= kMaxSmem;
 }
 
-template <int GQ>
+template <int GQ, int NH>
 int launch_fp8_gq(const CUtensorMap& tu, const Fp8Args& a, int smem, cudaStream_t stream) {
   static std::atomic<bool> cfg{false};
   if (!cfg.load()) {
-    if (cudaFuncSetAttribute(maxsim_fp8_kernel<GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+    if (cudaFuncSetAttribute(maxsim_fp8_kernel<GQ, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
       return FM_ERR_LAUNCH;
     cfg.store(true);
   }
   const int sms = sm_count();
   if (sms <= 0) return FM_ERR_NO_DEVICE;
-  maxsim_fp8_kernel<GQ><<<std::max(1, std::min(a.B, sms)), f8_threads(), smem, stream>>>(tu, a);
+  maxsim_fp8_kernel<GQ, NH><<<std::max(1, std::min(a.B, sms)), f8_threads(), smem, stream>>>(tu, a);
   return cudaGetLastError() == cudaSuccess ? FM_OK : FM_ERR_LAUNCH;
 }
 
@@ -688,7 +690,8 @@ int launch_fp8(const void* Q, const void* D8, const float* scales, const int32_t
                int Lq, int Ld, int d, int32_t* status, cudaStream_t stream, TopkArgs* topk) {
   Fp8Args a{};
   int smem = 0;
-  if (!plan_fp8(B, Lq, Ld, d, a, smem)) return FM_ERR_UNSUPPORTED;
+  const int nh = Lq <= 32 ? 2 : 1;
+  if (!plan_fp8(B, Lq, Ld, d, nh, a, smem)) return FM_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(scales) & 3u) != 0) return FM_ERR_ARG;
   a.lengths = lengths;
   a.scores = scores;
@@ -704,10 +707,10 @@ int launch_fp8(const void* Q, const void* D8, const float* scales, const int32_t
     a.topk = *topk;
   }
   CUtensorMap tu;
-  if (!make_map_3d(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D8, d, Ld, B, 128, kF8Tokens,
+  if (!make_map_3d(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D8, d, Ld, B, 128, nh * kF8Half,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return FM_ERR_LAUNCH;
-  return a.N == 96 ? launch_fp8_gq<1>(tu, a, smem, stream) : launch_fp8_gq<2>(tu, a, smem, stream);
+  return a.N == 96 ? launch_fp8_gq<1, 2>(tu, a, smem, stream) : launch_fp8_gq<2, 1>(tu, a, smem, stream);
 }
 
 }  // namespace

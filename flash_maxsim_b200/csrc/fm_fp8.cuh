@@ -8,10 +8,11 @@
 // (x ~= scale_t * code, scale_t = max|x_t| / 448): half the HBM bytes of
 // fp16 documents, no per-token min.
 //
-//  * The e4m3 codes are never converted.  TMA copies a 128-token chunk from
+//  * The e4m3 codes are never converted.  TMA copies a chunk of 256 tokens
+//    (128 for 64-row queries) from
 //    HBM into 128-byte-swizzled shared memory and the tensor core multiplies
 //    it as e4m3 (tcgen05.mma kind::f8f6f4, fp32 accumulate) with the chunk
-//    as the M = 128 operand.
+//    in 128-token halves as the M = 128 operand.
 //  * The fp16 query is split once per CTA into three e4m3 parts,
 //    Q / alpha ~= h + l + e with h = e4m3(x), l = e4m3(x - h),
 //    e = e4m3(x - h - l), x = Q / alpha, alpha = max|Q| / 448 (relative
@@ -42,7 +43,7 @@
 
 namespace fm {
 
-constexpr int kF8Tokens = 128;  // tokens per chunk (one TMA box per 128-byte K atom; the MMA's M)
+constexpr int kF8Half = 128;    // tokens per MMA (M); a chunk is NH of them (one TMA box per K atom)
 constexpr int kF8EW = 8;        // epilogue warps
 constexpr int kF8Xch = 8;       // per-document exchange slots of the epilogue
 constexpr int kF8Parts = 3;     // e4m3 parts of the query
@@ -94,10 +95,11 @@ __device__ __forceinline__ uint32_t e4m3_bits(float x) {
   return static_cast<uint32_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
 }
 
-template <int GQ>
+template <int GQ, int NH>
 __global__ void __launch_bounds__(f8_threads(), 1)
     maxsim_fp8_kernel(const __grid_constant__ CUtensorMap tmap_u, const Fp8Args a) {
   constexpr int EW = kF8EW;
+  constexpr int kF8Tokens = NH * kF8Half;  // tokens per chunk
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -207,11 +209,17 @@ __global__ void __launch_bounds__(f8_threads(), 1)
           if (!mbar_wait(t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) { ok = false; break; }
           tc_fence_after();
           const uint64_t au = smem_desc_sw128(sbase + a.off_u + ur.idx * a.u_slot_bytes);
-          const uint32_t tacc = tmem_base + tr.idx * a.N;
-          for (int at = 0; at < a.atoms; ++at) {
+          const uint32_t tacc = tmem_base + tr.idx * (NH * a.N);
+          // a 128-token half with no valid token is neither multiplied nor read
+          const int nhalf = min(NH, (f8_len(a, b) - c * kF8Tokens + kF8Half - 1) / kF8Half);
+          for (int hb = 0; hb < nhalf; ++hb) {
+            const uint64_t ah = au + hb * (kF8Half * 128u >> 4);
+            for (int at = 0; at < a.atoms; ++at) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per step, 4 steps per 128-byte atom
-              tc_mma_f8(tacc, au + at * u_atom + kk * 2u, bq + at * q_atom + kk * 2u, idesc, (at | kk) ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per step, 4 steps per 128-byte atom
+                tc_mma_f8(tacc + hb * a.N, ah + at * u_atom + kk * 2u, bq + at * q_atom + kk * 2u, idesc,
+                          (at | kk) ? 1u : 0u);
+            }
           }
           tc_commit(t_full(tr.idx));
           tc_commit(u_empty(ur.idx));
@@ -295,23 +303,34 @@ __global__ void __launch_bounds__(f8_threads(), 1)
           tr.next(a.nts);
           continue;
         }
-        const bool valid = c * kF8Tokens + tok < len;
-        // this token's scale, loaded before waiting for the accumulator
-        const float s_t = valid ? __ldg(a.scales + static_cast<size_t>(b) * a.Ld + c * kF8Tokens + tok) : 0.f;
+        // this thread's tokens' scales, loaded before waiting for the accumulator
+        float sa[NH];
+        bool valid[NH];
+#pragma unroll
+        for (int hb = 0; hb < NH; ++hb) {
+          valid[hb] = c * kF8Tokens + hb * kF8Half + tok < len;
+          sa[hb] = valid[hb]
+                       ? __ldg(a.scales + static_cast<size_t>(b) * a.Ld + c * kF8Tokens + hb * kF8Half + tok) * alpha
+                       : 0.f;
+        }
         if (!mbar_wait(t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t th = tmem_base + lane_base + tr.idx * a.N;
-        const float sa = s_t * alpha;
 #pragma unroll
-        for (int g = 0; g < GQ; ++g) {
-          float h[32], l[32], e[32];
-          tmem_ld32(th + g * 32, h);
-          tmem_ld32(th + R + g * 32, l);
-          tmem_ld32(th + 2 * R + g * 32, e);
-          tmem_wait_ld();
-          if (valid) {
+        for (int hb = 0; hb < NH; ++hb) {
+          if (!__any_sync(0xffffffffu, valid[hb])) continue;  // half not multiplied
+          const uint32_t th = tmem_base + lane_base + tr.idx * (NH * a.N) + hb * a.N;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) rmax[g * 32 + j] = fmaxf(rmax[g * 32 + j], sa * ((h[j] + l[j]) + e[j]));
+          for (int g = 0; g < GQ; ++g) {
+            float h[32], l[32], e[32];
+            tmem_ld32(th + g * 32, h);
+            tmem_ld32(th + R + g * 32, l);
+            tmem_ld32(th + 2 * R + g * 32, e);
+            tmem_wait_ld();
+            if (valid[hb]) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                rmax[g * 32 + j] = fmaxf(rmax[g * 32 + j], sa[hb] * ((h[j] + l[j]) + e[j]));
+            }
           }
         }
         tc_fence_before();
