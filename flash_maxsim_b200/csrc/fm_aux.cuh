@@ -232,9 +232,9 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd_kernel(
 // entries (slices in entry order), the counts become offsets in (token,
 // warp) order, and each warp scatters its slice in order -- so every bucket
 // lists its entries in ascending e, the same fixed summation order as the
-// single-warp sort.  Then each warp owns tokens t = w, w + 8, ...: it adds
-// g[n] * Q[e] over the bucket with four query-row gathers in flight and
-// writes the whole token row (zeros for untouched tokens).
+// single-warp sort.  Then each warp streams the entries of a contiguous,
+// entry-balanced range of tokens (see the accumulation below) and writes
+// whole token rows (zeros for untouched tokens).
 // Shared memory: cnt[8][Ld + 1] + base[Ld + 2] + order[Nq * Lq] ints,
 // g of each sorted entry [Nq * Lq] and g[Nq] floats.
 constexpr int kDdWarps = kBwdThreads / 32;
@@ -336,36 +336,69 @@ __global__ void __launch_bounds__(kBwdThreads) maxsim_bwd_dd2_kernel(
     __syncwarp();
   }
   __syncthreads();
+  // Accumulation: the tokens that hold entries, [0, t_end), are cut into 8
+  // contiguous ranges with about equal entry counts (whole tokens); each warp
+  // streams its range's entries in order with eight gathers in flight across
+  // token boundaries, writing each token row as it completes (zero rows
+  // included).  Tokens [t_end, Ld) hold no entry: all warps write their zero
+  // rows in turn.  Each token's sum keeps the ascending entry order.
+  const int etot = base[Ld];
+  auto lower_bound = [&](int v) {  // first token t with base[t] >= v (base is non-decreasing)
+    int lo = 0, hi = Ld;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (base[mid] < v) lo = mid + 1;
+      else hi = mid;
+    }
+    return lo;
+  };
+  const int t_end = lower_bound(etot);  // tokens past the last one that has an entry
+  const int t_lo = warp == 0 ? 0 : min(lower_bound(static_cast<int>(static_cast<int64_t>(etot) * warp / kDdWarps)), t_end);
+  const int t_hi = warp == kDdWarps - 1 ? t_end
+                                        : min(lower_bound(static_cast<int>(static_cast<int64_t>(etot) * (warp + 1) / kDdWarps)), t_end);
   const int nseg = (d + 255) / 256;
-  for (int t = warp; t < Ld; t += kDdWarps) {
-    const int beg = base[t], end = base[t + 1];
-    __half* out = dD + (static_cast<size_t>(b) * Ld + t) * d;
-    for (int s = 0; s < nseg; ++s) {
-      const int k = s * 256 + lane * 8;
-      const bool kin = k < d;
-      float acc[8];
+  constexpr int U = 8;
+  for (int s = 0; s < nseg; ++s) {
+    const int k = s * 256 + lane * 8;
+    const bool kin = k < d;
+    __half* out0 = dD + static_cast<size_t>(b) * Ld * d + k;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    int t = t_lo;
+    const int p_end = t_hi > t_lo ? base[t_hi] : base[t_lo];
+    for (int p0 = t_hi > t_lo ? base[t_lo] : p_end; p0 < p_end; p0 += U) {
+      uint4 raw[U];
+      float gv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const bool in = p0 + u < p_end;
+        const int e = in ? order[p0 + u] : 0;
+        gv[u] = in ? gsort[p0 + u] : 0.f;
+        raw[u] = (in && kin) ? __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k))
+                             : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int pp = p0 + u;
+        if (pp >= p_end) break;
+        while (pp >= base[t + 1]) {  // token t is complete
+          if (kin) *reinterpret_cast<uint4*>(out0 + static_cast<size_t>(t) * d) = pack8(acc);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+          ++t;
+        }
+        fma8(acc, raw[u], gv[u]);
+      }
+    }
+    for (; t < t_hi; ++t) {  // the range's last token, and any empty ones before it
+      if (kin) *reinterpret_cast<uint4*>(out0 + static_cast<size_t>(t) * d) = pack8(acc);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      int p = beg;
-      for (; p + 4 <= end; p += 4) {
-        uint4 raw[4];
-        float gv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = order[p + u];
-          gv[u] = gsort[p + u];
-          raw[u] = kin ? __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k))
-                       : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) fma8(acc, raw[u], gv[u]);
-      }
-      for (; p < end; ++p) {
-        const int e = order[p];
-        if (kin) fma8(acc, __ldg(reinterpret_cast<const uint4*>(Q + static_cast<size_t>(e) * d + k)), gsort[p]);
-      }
-      if (kin) *reinterpret_cast<uint4*>(out + k) = pack8(acc);
     }
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int tz = t_end + warp; tz < Ld; tz += kDdWarps)
+      if (kin) *reinterpret_cast<uint4*>(out0 + static_cast<size_t>(tz) * d) = z;
   }
 }
 
