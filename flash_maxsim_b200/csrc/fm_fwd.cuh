@@ -549,6 +549,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
       const int ksteps = a.kq_atoms * 4;  // K=16 steps per Q stage (4 or 8)
       const uint32_t b_atom = a.C * 8u;    // one K atom of a D slot, in 16-byte units
       const bool skip_mma = FM_DBG(a, 2);
+      [[maybe_unused]] const int ich = me == 0 ? 0 : 5;  // trace channel of this issuer (FM_TRACE)
       Ring dr, qr, tr;
       bool ok = true;
       FM_TR_DECL;
@@ -562,7 +563,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
             const int cn = group_chunks(a, it, g);
             {
               Ring r = dr;
-              FM_TR(0, 8);
+              FM_TR(ich, 8);
               for (int c = 0; c < cn; ++c) {
                 if (!mbar_wait(bars.d_full(r.idx), r.phase, ctl, FM_ERR_TIMEOUT_DFULL)) {
                   ok = false;
@@ -570,7 +571,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                 }
                 r.next(a.nd);
               }
-              FM_TR(0, 9);
+              FM_TR(ich, 9);
             }
             if (!ok) break;
             tc_fence_after();
@@ -578,13 +579,13 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
               if (a.nk == 1) {
                 const int qslot = a.q_resident ? 0 : qr.idx;
                 const uint32_t qph = a.q_resident ? 0u : qr.phase;
-                FM_TR(0, 5);
+                FM_TR(ich, 5);
                 if (!(FM_DBG(a, 1024) && qr.phase) && !(FM_DBG(a, 256) && mbar_test_wait(bars.q_full(qslot), qph)) &&
                     !mbar_wait(bars.q_full(qslot), qph, ctl, FM_ERR_TIMEOUT_QFULL)) {
                   ok = false;
                   break;
                 }
-                FM_TR(0, 6);
+                FM_TR(ich, 6);
                 tc_fence_after();
                 const uint64_t adesc = smem_desc_sw128(sbase + a.off_q + qslot * a.q_stage_bytes);
                 Ring r = dr;
@@ -597,13 +598,13 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     r.next(a.nd);
                     continue;
                   }
-                  FM_TR(0, 1);
+                  FM_TR(ich, 1);
                   if (!FM_DBG(a, 512) && !(FM_DBG(a, 256) && mbar_test_wait(bars.t_empty(tr.idx), tr.phase ^ 1u)) &&
                       !mbar_wait(bars.t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) {
                     ok = false;
                     break;
                   }
-                  FM_TR(0, 2);
+                  FM_TR(ich, 2);
                   tc_fence_after();
                   const uint64_t bdesc = smem_desc_sw128(sbase + a.off_d + r.idx * a.d_slot_bytes);
                   const uint32_t tacc = tmem_base + tr.idx * a.ts_stride;
@@ -620,9 +621,9 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                     }
                   }
                   FM_PROF_ADD(20, pm0);
-                  FM_TR(0, 3);
+                  FM_TR(ich, 3);
                   tc_commit(bars.t_full(tr.idx));
-                  FM_TR(0, 4);
+                  FM_TR(ich, 4);
                   tr.next(a.nts);
                   r.next(a.nd);
                 }
@@ -631,7 +632,7 @@ __global__ void __launch_bounds__(MODE == MODE_INT8 ? kThreadsI8 : kThreadsF16, 
                   tc_commit(bars.q_empty(qr.idx));
                   qr.next(a.nq);
                 }
-                FM_TR(0, 7);
+                FM_TR(ich, 7);
               } else {
                 // K split over several Q stages (single-document items only):
                 // every chunk slot of this M-block stays live until the last stage.
