@@ -401,9 +401,9 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   a.u_slot_bytes = a.atoms * kI8Tokens * 128u;
   a.sc_slot_bytes = 2 * round_up(kI8Tokens * 2 + 32, 16);
   const int q_bytes = a.atoms * a.N * 128;
-  const int misc = round_up((64 + 64 + kI8Xch * 8 * gq * 32) * 4 + 2 * kI8Xch * 4, 16);
+  const int misc = round_up((64 + 64 + kI8Xch * 8 * gq * 32) * 4, 16);
   const int per_slot = static_cast<int>(a.u_slot_bytes + a.sc_slot_bytes) + 16;
-  const int fixed = 1024 + round_up(q_bytes, 1024) + misc + (2 * a.nts + 2) * 8 + 32;
+  const int fixed = 1024 + round_up(q_bytes, 1024) + misc + (2 * a.nts + 2 + 2 * kI8Xch) * 8 + 32;
   a.nu = std::min(16, (kMaxSmem - fixed) / per_slot);
   if (tune().nd > 0) a.nu = std::min(a.nu, tune().nd);
   a.nu &= ~1;  // even: paired epilogue warps and MMA issuers own alternate slots
@@ -418,7 +418,7 @@ bool plan_int8_fast(int B, int Lq, int Ld, int d, Int8Args& a, int& smem) {
   a.off_misc = round_up(off, 16);
   off = a.off_misc + misc;
   a.off_bar = round_up(off, 16);
-  off = a.off_bar + (2 * a.nu + 2 * a.nts + 2) * 8 + 32;
+  off = a.off_bar + (2 * a.nu + 2 * a.nts + 2 + 2 * kI8Xch) * 8 + 32;
   smem = std::max(static_cast<int>(off) + 1024, kMinSmem);
   return smem <= kMaxSmem;
 }

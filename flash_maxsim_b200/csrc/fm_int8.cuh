@@ -25,7 +25,11 @@
 //    with the chunk.  The four warps' maxima are combined per document.
 //
 // Warp roles: 0 = producer (TMA + bulk copies), 1 = MMA issuer + TMEM owner,
-// 2..5 = epilogue (also build the split query).
+// 2.. = epilogue (also build the split query), (a second MMA issuer with 8
+// epilogue warps), last = combiner: the epilogue warps hand each document's
+// per-warp row maxima over through an mbarrier-guarded exchange slot and go
+// on to the next document; the combiner takes the maximum over warps, sums the
+// query rows and writes the score.
 #pragma once
 
 #include <cuda.h>
@@ -38,8 +42,10 @@ namespace fm {
 
 // two warps + 4 or 8 epilogue warps (8: two per TMEM lane quarter taking
 // alternate chunks, so every scheduler has two independent epilogue warps)
-// (with 8 epilogue warps a second MMA issuer follows them: warp 10)
-__host__ __device__ constexpr int i8_threads(int epi_warps) { return (2 + epi_warps + (epi_warps == 8 ? 1 : 0)) * 32; }
+// (with 8 epilogue warps a second MMA issuer follows them: warp 10), then the
+// combiner warp that sums each document's row maxima
+__host__ __device__ constexpr int i8_combiner_warp(int epi_warps) { return 2 + epi_warps + (epi_warps == 8 ? 1 : 0); }
+__host__ __device__ constexpr int i8_threads(int epi_warps) { return (i8_combiner_warp(epi_warps) + 1) * 32; }
 #ifndef FM_I8_TOKENS
 #define FM_I8_TOKENS 256
 #endif
@@ -108,7 +114,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // barriers: u_full[nu] u_empty[nu] t_full[nts] t_empty[nts] q_ready drain
+  // barriers: u_full[nu] u_empty[nu] t_full[nts] t_empty[nts] q_ready drain x_full[kI8Xch] x_empty[kI8Xch]
   const uint32_t bar0 = sbase + a.off_bar;
   auto u_full = [&](int i) { return bar0 + 8u * i; };
   auto u_empty = [&](int i) { return bar0 + 8u * (a.nu + i); };
@@ -116,7 +122,9 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
   auto t_empty = [&](int i) { return bar0 + 8u * (2 * a.nu + a.nts + i); };
   const uint32_t q_ready = bar0 + 8u * (2 * a.nu + 2 * a.nts);
   const uint32_t drain = q_ready + 8u;
-  uint8_t* ctl_area = smem + a.off_bar + 8 * (2 * a.nu + 2 * a.nts + 2);
+  auto x_full = [&](int i) { return drain + 8u + 8u * i; };
+  auto x_empty = [&](int i) { return drain + 8u + 8u * (kI8Xch + i); };
+  uint8_t* ctl_area = smem + a.off_bar + 8 * (2 * a.nu + 2 * a.nts + 2 + 2 * kI8Xch);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(ctl_area);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctl_area + 8);
   WaitCtl ctl{abort_flag, a.status, a.timeout_ns};
@@ -124,8 +132,6 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
   float* a256_s = reinterpret_cast<float*>(smem + a.off_misc);  // [64] alpha / 256 per query row
   float* qsum_s = a256_s + 64;                                   // [64]
   float* xch = qsum_s + 64;                                      // [kI8Xch docs][EW warps][GQ][32]
-  int* cnt = reinterpret_cast<int*>(xch + kI8Xch * EW * GQ * 32); // [kI8Xch] arrivals
-  volatile int* done = cnt + kI8Xch;                             // [kI8Xch] combined generations
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.nu; ++i) {
@@ -138,11 +144,11 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
     }
     mbar_init(q_ready, EW);
     mbar_init(drain, EW == 8 ? 2 : 1);  // every MMA issuer commits
-    *abort_flag = 0;
     for (int i = 0; i < kI8Xch; ++i) {
-      cnt[i] = 0;
-      done[i] = 0;
+      mbar_init(x_full(i), EW);  // every epilogue warp's row maxima of the document
+      mbar_init(x_empty(i), 1);  // the combiner has read the slot
     }
+    *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -159,6 +165,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
   if (warp == 0) {
     // ===================== producer =====================
     if (lane == 0) {
+      FM_TR_DECL;
       const uint64_t pol = l2_policy_evict_first();
       const uint32_t tx = a.atoms * kI8Tokens * 128u;
       Ring ur;
@@ -168,10 +175,12 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         const int len = i8_len(a, b);
         const int nch = (len + kI8Tokens - 1) / kI8Tokens;
         for (int c = 0; c < nch; ++c) {
+          FM_TR(4, 1);
           if (!mbar_wait(u_empty(ur.idx), ur.phase ^ 1u, ctl, FM_ERR_TIMEOUT_UEMPTY)) {
             ok = false;
             break;
           }
+          FM_TR(4, 2);
           // uint8 tile by TMA; the chunk's fp16 scales and mins by two bulk copies
           // of the enclosing 16-byte-aligned spans (staging: [scales span][mins span])
           const size_t e0 = static_cast<size_t>(b) * a.Ld + static_cast<size_t>(c) * kI8Tokens;
@@ -204,6 +213,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
             bulk_load(st + a.sc_slot_bytes / 2, reinterpret_cast<const uint8_t*>(a.mins) + lo16, span,
                       u_full(ur.idx), pol);
           }
+          FM_TR(4, 3);
           ur.next(a.nu);
           ++issued;
         }
@@ -223,6 +233,8 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
     // a TMEM slot and of a staging slot is handled by the same issuer.
     if (lane == 0) {
       const int me = warp == 1 ? 0 : 1;
+      [[maybe_unused]] const int ich = me == 0 ? 0 : 5;  // trace channel of this issuer (FM_TRACE)
+      FM_TR_DECL;
       // A = uint8 chunk (unsigned, M = 128 tokens), B = split query (signed, N rows)
       const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) |
                              (static_cast<uint32_t>(a.N >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
@@ -243,8 +255,11 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
           }
           // a half with no valid token is neither multiplied nor read by the epilogue
           const int nhalf = min(kI8Halves, (len - c * kI8Tokens + kI8Half - 1) / kI8Half);
+          FM_TR(ich, 1);
           if (!mbar_wait(u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
+          FM_TR(ich, 2);
           if (!mbar_wait(t_empty(tr.idx), tr.phase ^ 1u, ctl, FM_ERR_TIMEOUT_TEMPTY)) { ok = false; break; }
+          FM_TR(ich, 3);
           tc_fence_after();
           FM_PROF_T0(pm0);
           const uint64_t au = smem_desc_sw128(sbase + a.off_u + ur.idx * a.u_slot_bytes);
@@ -260,6 +275,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
           }
           tc_commit(t_full(tr.idx));
           tc_commit(u_empty(ur.idx));
+          FM_TR(ich, 4);
           FM_PROF_ADD(20, pm0);
           tr.next(a.nts);
           ur.next(a.nu);
@@ -341,6 +357,9 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     const int tok_in_chunk = sub * 32 + lane;
     Ring ur, tr;
+    // trace channels (FM_TRACE): 1 and 2 = the two warps of lane quarter 0, 3 = a warp of quarter 2
+    [[maybe_unused]] const int ech = sub == 0 ? 1 + half : (sub == 2 && half == 0 ? 3 : 7);
+    FM_TR_DECL;
     int dloc = 0;
     int kglob = 0;  // chunk counter of this CTA
     bool ok = true;
@@ -359,8 +378,10 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         }
         // u_full also publishes the chunk's scales/mins; the slot is not refilled
         // before this warp releases it below
+        if (ech < 7) FM_TR(ech, 1);
         if (!mbar_wait(u_full(ur.idx), ur.phase, ctl, FM_ERR_TIMEOUT_UFULL)) { ok = false; break; }
         if (!mbar_wait(t_full(tr.idx), tr.phase, ctl, FM_ERR_TIMEOUT_TFULL)) { ok = false; break; }
+        if (ech < 7) FM_TR(ech, 2);
         tc_fence_after();
         FM_PROF_T0(pe0);
         const size_t byte0 = (static_cast<size_t>(b) * a.Ld + static_cast<size_t>(c) * kI8Tokens) * 2;
@@ -392,6 +413,7 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
             }
           }
         }
+        if (ech < 7) FM_TR(ech, 3);
         FM_PROF_ADD(22 + sub, pe0);
         tc_fence_before();
         __syncwarp();
@@ -409,55 +431,42 @@ __global__ void __launch_bounds__(i8_threads(EW), 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = rmax[g * 32 + j];
-        acc[g] = butterfly_max32(v, lane);
+        acc[g] = colmax32(v, lane);
       }
-      // --- combine the four warps of this document: the last one to arrive sums ---
+      if (ech < 7) FM_TR(ech, 5);
+      // --- hand the row maxima to the combiner: wait until it has read this
+      //     exchange slot's previous document (parity of the slot's last use) ---
       const int slot = dloc % kI8Xch;
-      const int gen = dloc / kI8Xch;
-      // a warp can run ahead (short or empty documents): wait until the slot's
-      // previous document has been combined
-      if (gen > 0) {
-        const uint64_t t0 = globaltimer_ns();
-        while (done[slot] < gen) {
-          if (*abort_flag) { ok = false; break; }
-          if (globaltimer_ns() - t0 > a.timeout_ns) {
-            *abort_flag = 1;
-            record_status(a.status, FM_ERR_TIMEOUT_TFULL);
-            ok = false;
-            break;
-          }
-        }
-        if (!ok) break;
-        __threadfence_block();
-      }
+      const uint32_t xpar = static_cast<uint32_t>(dloc / kI8Xch) & 1u;
+      if (!mbar_wait(x_empty(slot), xpar ^ 1u, ctl, FM_ERR_TIMEOUT_TFULL)) break;
+      if (ech < 7) FM_TR(ech, 6);
       const int ew = warp - 2;
 #pragma unroll
       for (int g = 0; g < GQ; ++g) xch[((slot * EW + ew) * GQ + g) * 32 + lane] = acc[g];
       __syncwarp();
-      int old = 0;
-      if (lane == 0) {
-        __threadfence_block();
-        old = atomicAdd(&cnt[slot], 1);
-      }
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == EW - 1) {
-        __threadfence_block();
-        float tot = 0.f;
+      if (lane == 0) mbar_arrive(x_full(slot));
+      if (ech < 7) FM_TR(ech, 7);
+    }
+  } else if (warp == i8_combiner_warp(EW)) {
+    // ===================== combiner =====================
+    // lane = query row of a 32-row group: max over the epilogue warps, then the
+    // sum over the query's rows (the same order as a one-warp reduction)
+    int dloc = 0;
+    for (int b = w0; b < a.B; b += wstep, ++dloc) {
+      const int slot = dloc % kI8Xch;
+      const uint32_t xpar = static_cast<uint32_t>(dloc / kI8Xch) & 1u;
+      if (!mbar_wait(x_full(slot), xpar, ctl, FM_ERR_TIMEOUT_TFULL)) break;
+      float tot = 0.f;
 #pragma unroll
-        for (int g = 0; g < GQ; ++g) {
-          float mm = -INFINITY;
-          for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
-          tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
-        }
-        tot = warp_sum(tot);
-        if (lane == 0) {
-          a.scores[b] = tot;
-          cnt[slot] = 0;
-          __threadfence_block();
-          done[slot] = gen + 1;
-        }
-        __syncwarp();
+      for (int g = 0; g < GQ; ++g) {
+        float mm = -INFINITY;
+        for (int w = 0; w < EW; ++w) mm = fmaxf(mm, xch[((slot * EW + w) * GQ + g) * 32 + lane]);
+        tot += (g * 32 + lane < a.Lq) ? mm : 0.f;
       }
+      tot = warp_sum(tot);
+      if (lane == 0) a.scores[b] = tot;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(x_empty(slot));
     }
   }
 

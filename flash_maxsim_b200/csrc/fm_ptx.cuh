@@ -345,4 +345,38 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// Two fp32 fused multiply-adds in one instruction (sm_100 fma.rn.f32x2):
+// (d0, d1) = (a0 * b0 + c0, a1 * b1 + c1), each rounded once.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+  uint64_t a, b, c, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+// Maximum over the 32 lanes of one float, returned to every lane
+// (sm_100a: redux.sync on f32).
+__device__ __forceinline__ float warp_max_f32(float x) {
+  float r;
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Column maxima of a 32 x 32 tile held one row per lane (v[j] = column j):
+// one warp reduction per column, then lane j picks column j's maximum by a
+// five-level select tree.  Replaces a 31-shuffle transpose-and-max butterfly.
+__device__ __forceinline__ float colmax32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = warp_max_f32(v[j]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < o; ++i) v[i] = (lane & o) ? v[i + o] : v[i];
+  }
+  return v[0];
+}
+
 }  // namespace fm
