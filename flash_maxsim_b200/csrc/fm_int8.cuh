@@ -20,9 +20,9 @@
 //    owns one token: it applies, in fp32,
 //      S[t, q] = scale_t * alpha_q * (256 <h,u> + <l,u>) / 256 + min_t * sum_k Q[q, k]
 //    (256 <h,u> + <l,u> is an exact integer), masks tokens past the document,
-//    and a 31-shuffle butterfly leaves lane j with the max over the warp's
-//    32 tokens for query row j.  Per-token scale/min arrive by bulk copy
-//    with the chunk.  The four warps' maxima are combined per document.
+//    and at the end of a document one warp reduction per query row
+//    (redux.sync.max.f32) leaves lane j with the max over the warp's tokens
+//    for query row j.  Per-token scale/min arrive by bulk copy with the chunk.
 //
 // Warp roles: 0 = producer (TMA + bulk copies), 1 = MMA issuer + TMEM owner,
 // 2.. = epilogue (also build the split query), (a second MMA issuer with 8
@@ -80,6 +80,7 @@ __device__ __forceinline__ int i8_len(const Int8Args& a, int b) {
 
 // Max over the 32 lanes of v[j] for every j; afterwards lane j's v[0] holds
 // column j's maximum.  Lanes with bit o set keep the upper half at offset o.
+// (The FP8 kernel's per-document reduction.)
 __device__ __forceinline__ float butterfly_max32(float (&v)[32], int lane) {
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {

@@ -367,7 +367,8 @@ __device__ __forceinline__ float warp_max_f32(float x) {
 
 // Column maxima of a 32 x 32 tile held one row per lane (v[j] = column j):
 // one warp reduction per column, then lane j picks column j's maximum by a
-// five-level select tree.  Replaces a 31-shuffle transpose-and-max butterfly.
+// five-level select tree (fewer and shorter dependent steps than a
+// 31-shuffle transpose-and-max butterfly).
 __device__ __forceinline__ float colmax32(float (&v)[32], int lane) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = warp_max_f32(v[j]);
