@@ -87,6 +87,28 @@ def test_fullsize_int8(cuda):
     _assert_ok(SC.check_int8(_np(Q), _np(u8[it]), _np(sc[it]), _np(mn[it]), _np(got[it])))
 
 
+@pytest.mark.parametrize("Lq", [32, 64])
+def test_int8_many_docs_per_cta_varlen(cuda, Lq):
+    # the short-query INT8 kernel's per-document exchange slots (8 per CTA)
+    # wrap many times: 3000 documents over 148 CTAs, ragged lengths with
+    # empty documents, for both epilogue layouts (8 warps for 32 query rows,
+    # 4 warps for 64)
+    import flash_maxsim_b200 as fm
+    B, Ld, d = 3000, 300, 128
+    Q = synth((Lq, d), 16 + Lq, cuda)
+    D = synth((B, Ld, d), 17, cuda)
+    u8, sc, mn = fm.quantize_int8(D)
+    del D
+    lens = np.random.default_rng(Lq).integers(0, Ld + 1, B).astype(np.int32)
+    idx = SC.sample_docs(B, 256, seed=9)
+    lens[idx[::5]] = 0
+    lens[idx[1::5]] = 44  # as long as the tail chunk of a 300-token document
+    got = fm.flash_maxsim_int8(Q, u8, sc, mn, torch.from_numpy(lens).to(cuda))
+    fm.check_status(cuda)
+    it = torch.from_numpy(idx).to(cuda)
+    _assert_ok(SC.check_int8(_np(Q), _np(u8[it]), _np(sc[it]), _np(mn[it]), _np(got[it]), lens[idx]))
+
+
 def test_fullsize_train(cuda):
     # config 5 shapes: Nq=64, Lq=64, d=256, Ld=1024, lengths U[32, 1024], 600 docs
     import flash_maxsim_b200 as fm
