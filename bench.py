@@ -567,7 +567,7 @@ def run_e2e(args, w: Workload, fm, sharded, world, dev):
         dD = [torch.empty_like(w.Du8), torch.empty_like(w.sc)]
     else:
         hD = [w.D.cpu().pin_memory()]
-        dD = [torch.empty_like(w.D)]
+        dD = [] if kind == "batched" else [torch.empty_like(w.D)]
     hL = w.lengths.cpu().pin_memory() if w.lengths is not None else None
     h2d = hQ.numel() * hQ.element_size() + sum(t.numel() * t.element_size() for t in hD)
     if hL is not None:
@@ -577,14 +577,26 @@ def run_e2e(args, w: Workload, fm, sharded, world, dev):
 
     def one():
         nonlocal out_host, d2h
+        if kind == "batched":
+            # the public host-corpus entry point: the documents cross PCIe in
+            # pieces on a copy stream while the pieces already copied are scored
+            out = fm.flash_maxsim_batched_from_host(hQ, hD[0], hL, device=dev)
+        else:
+            out = step_from_device_copies()
+        if world > 1:
+            out = sharded.all_gather_scores(out if out.dim() == 2 else out.unsqueeze(0), w.B)
+        if out_host is None:
+            out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            d2h = out.numel() * out.element_size()
+        out_host.copy_(out, non_blocking=True)
+
+    def step_from_device_copies():
         q = hQ.to(dev, non_blocking=True)
         for h, dd in zip(hD, dD):
             dd.copy_(h, non_blocking=True)
         ln = hL.to(dev, non_blocking=True) if hL is not None else None
         if kind == "single":
             out = fm.flash_maxsim(q, dD[0])
-        elif kind == "batched":
-            out = fm.flash_maxsim_batched(q, dD[0])
         elif kind == "int8":
             out = fm.flash_maxsim_int8(q, dD[0], dD[1], dD[2])
         elif kind == "fp8":
@@ -596,12 +608,7 @@ def run_e2e(args, w: Workload, fm, sharded, world, dev):
             s.backward(w.grad)
             out = s.detach()
             dD[0] = dg.detach()
-        if world > 1:
-            out = sharded.all_gather_scores(out if out.dim() == 2 else out.unsqueeze(0), w.B)
-        if out_host is None:
-            out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-            d2h = out.numel() * out.element_size()
-        out_host.copy_(out, non_blocking=True)
+        return out
 
     one()
     torch.cuda.synchronize(dev)

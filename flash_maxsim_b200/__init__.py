@@ -10,6 +10,7 @@ from ._lib import check_status, LOADED_PATH  # noqa: F401  (loads the CUDA libra
 from .api import (  # noqa: F401
     flash_maxsim,
     flash_maxsim_batched,
+    flash_maxsim_batched_from_host,
     flash_maxsim_topk,
     flash_maxsim_batched_topk,
     flash_maxsim_packed,
@@ -30,6 +31,7 @@ from .api import (  # noqa: F401
 __all__ = [
     "flash_maxsim",
     "flash_maxsim_batched",
+    "flash_maxsim_batched_from_host",
     "flash_maxsim_topk",
     "flash_maxsim_batched_topk",
     "flash_maxsim_packed",

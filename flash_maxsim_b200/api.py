@@ -153,6 +153,82 @@ def flash_maxsim_batched(Q: torch.Tensor, D: torch.Tensor, doc_lengths=None,
     return scores
 
 
+_copy_streams: dict = {}
+
+
+def _copy_stream(device) -> torch.cuda.Stream:
+    """One host-to-device copy stream per device, created on first use."""
+    idx = torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    if idx not in _copy_streams:
+        _copy_streams[idx] = torch.cuda.Stream(device=idx)
+    return _copy_streams[idx]
+
+
+def flash_maxsim_batched_from_host(Q: torch.Tensor, D_host: torch.Tensor, doc_lengths=None,
+                                   piece_bytes: int = 512 << 20, nbuf: int = 3,
+                                   device=None) -> torch.Tensor:
+    """flash_maxsim_batched over shared documents that stay in host memory:
+    Q [Nq, Lq, d] (host or device), D_host [B, Ld, d] on the CPU -> [Nq, B]
+    fp32 on the GPU (`device`, else Q's device if it is a CUDA tensor, else
+    the current device).
+
+    The documents cross PCIe in pieces of about `piece_bytes` on a copy
+    stream, through `nbuf` device buffers, while the pieces already copied
+    are scored on the current stream: the copies hide the scoring, and the
+    GPU holds nbuf pieces instead of the whole corpus (a corpus larger than
+    device memory can be scored). Each document is scored on its own, so the
+    scores equal flash_maxsim_batched's on the whole corpus. D_host should be
+    pinned (`pin_memory()`); from pageable memory every copy waits for the
+    host and nothing overlaps. The call returns once everything is enqueued.
+    """
+    if device is None:
+        device = Q.device if Q.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    dev = torch.device(device)
+    if D_host.is_cuda:
+        return flash_maxsim_batched(Q.to(dev), D_host, doc_lengths)
+    assert Q.dim() == 3 and D_host.dim() == 3 and Q.shape[2] == D_host.shape[2]
+    assert nbuf >= 1 and piece_bytes >= 1
+    Nq, Lq, d = Q.shape
+    B, Ld, _ = D_host.shape
+    q = Q.to(dev, non_blocking=True)
+    lengths = None
+    if doc_lengths is not None:
+        lengths = torch.as_tensor(doc_lengths).to(dev, non_blocking=True)
+        assert lengths.numel() == B, "doc_lengths needs one entry per document"
+    per_doc = max(1, Ld * d * D_host.element_size())
+    piece = max(1, min(B, piece_bytes // per_doc))
+    npieces = (B + piece - 1) // piece
+    if Nq == 0 or npieces <= 1:
+        D = D_host.to(dev, non_blocking=True)
+        return flash_maxsim_batched(q, D, lengths)
+    out = torch.empty(Nq, B, dtype=torch.float32, device=dev)
+    main = torch.cuda.current_stream(dev)
+    cs = _copy_stream(dev)
+    cs.wait_stream(main)  # the buffers below may reuse memory that queued work still reads
+    bufs = [torch.empty((piece, Ld, d), dtype=D_host.dtype, device=dev)
+            for _ in range(min(nbuf, npieces))]
+    freed = [None] * len(bufs)  # event after the last scoring that read each buffer
+    for i in range(npieces):
+        b0 = i * piece
+        b1 = min(B, b0 + piece)
+        k = i % len(bufs)
+        buf = bufs[k][:b1 - b0]
+        with torch.cuda.stream(cs):
+            if freed[k] is not None:
+                cs.wait_event(freed[k])
+            buf.copy_(D_host[b0:b1], non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(cs)
+        main.wait_event(ready)
+        out[:, b0:b1] = flash_maxsim_batched(q, buf, None if lengths is None else lengths[b0:b1])
+        ev = torch.cuda.Event()
+        ev.record(main)
+        freed[k] = ev
+    return out
+
+
 # ---------------------------------------------------------------------------
 # packed (unpadded) documents
 # ---------------------------------------------------------------------------

@@ -146,3 +146,23 @@ def test_empty_batch(cuda):
     Q, D = O.seeded_inputs(15, (32, 128), (1, 8, 128))
     out = fm.flash_maxsim(dev(Q, cuda), dev(D, cuda)[:0])
     assert out.shape == (0,)
+
+
+@pytest.mark.parametrize("pinned,lengths", [(True, True), (True, False), (False, True)])
+def test_batched_from_host_streams_pieces(cuda, pinned, lengths):
+    # documents in host memory, copied in ~23 pieces through two device
+    # buffers while earlier pieces are scored: the same scores as one call on
+    # the whole device-resident corpus, and the oracle agrees
+    import flash_maxsim_b200 as fm
+    Q, D = O.seeded_inputs(31, (3, 32, 128), (3000, 300, 128))
+    lens = np.random.default_rng(5).integers(0, 301, 3000).astype(np.int32) if lengths else None
+    hD = torch.from_numpy(D).half()
+    if pinned:
+        hD = hD.pin_memory()
+    hQ = torch.from_numpy(Q).half()
+    want = fm.flash_maxsim_batched(hQ.to(cuda), hD.to(cuda), None if lens is None else dev(lens, cuda))
+    got = fm.flash_maxsim_batched_from_host(hQ, hD, None if lens is None else torch.from_numpy(lens),
+                                            piece_bytes=10 << 20, nbuf=2, device=cuda)
+    assert got.device == want.device
+    assert torch.equal(got, want)
+    close(got[:, :200].cpu(), O.maxsim_batched(Q, D[:200], None if lens is None else lens[:200]))
