@@ -166,6 +166,14 @@ def _copy_stream(device) -> torch.cuda.Stream:
     return _copy_streams[idx]
 
 
+def host_pieces(B: int, doc_bytes: int, piece_bytes: int) -> tuple[int, int]:
+    """Documents per piece and number of pieces for streaming B documents of
+    doc_bytes each in pieces of at most piece_bytes (at least one document
+    per piece; piece i covers documents [i * piece, min(B, (i + 1) * piece)))."""
+    piece = max(1, min(B, piece_bytes // max(1, doc_bytes)))
+    return piece, (B + piece - 1) // piece
+
+
 def flash_maxsim_batched_from_host(Q: torch.Tensor, D_host: torch.Tensor, doc_lengths=None,
                                    piece_bytes: int = 512 << 20, nbuf: int = 3,
                                    device=None) -> torch.Tensor:
@@ -197,9 +205,7 @@ def flash_maxsim_batched_from_host(Q: torch.Tensor, D_host: torch.Tensor, doc_le
     if doc_lengths is not None:
         lengths = torch.as_tensor(doc_lengths).to(dev, non_blocking=True)
         assert lengths.numel() == B, "doc_lengths needs one entry per document"
-    per_doc = max(1, Ld * d * D_host.element_size())
-    piece = max(1, min(B, piece_bytes // per_doc))
-    npieces = (B + piece - 1) // piece
+    piece, npieces = host_pieces(B, Ld * d * D_host.element_size(), piece_bytes)
     if Nq == 0 or npieces <= 1:
         D = D_host.to(dev, non_blocking=True)
         return flash_maxsim_batched(q, D, lengths)
@@ -211,8 +217,7 @@ def flash_maxsim_batched_from_host(Q: torch.Tensor, D_host: torch.Tensor, doc_le
             for _ in range(min(nbuf, npieces))]
     freed = [None] * len(bufs)  # event after the last scoring that read each buffer
     for i in range(npieces):
-        b0 = i * piece
-        b1 = min(B, b0 + piece)
+        b0, b1 = i * piece, min(B, (i + 1) * piece)
         k = i % len(bufs)
         buf = bufs[k][:b1 - b0]
         with torch.cuda.stream(cs):

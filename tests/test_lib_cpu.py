@@ -105,3 +105,21 @@ def test_reference_helpers_are_plain_torch():
     Q, D = O.seeded_inputs(0, (8, 16), (3, 5, 16))
     got = fm.maxsim_naive(torch.from_numpy(Q), torch.from_numpy(D)).numpy()
     assert abs(got - O.maxsim(Q, D)).max() < 1e-4
+
+
+def test_host_streaming_pieces_cover_the_corpus():
+    # flash_maxsim_batched_from_host's piece plan: contiguous, disjoint,
+    # covering [0, B), each piece within the byte budget unless one document
+    # alone exceeds it
+    from flash_maxsim_b200.api import host_pieces
+    for B, doc, budget in [(100000, 300 * 128 * 2, 512 << 20), (3000, 76800, 10 << 20), (7, 10, 1),
+                           (1, 1 << 30, 512 << 20), (5, 100, 1000), (0, 100, 1000)]:
+        piece, n = host_pieces(B, doc, budget)
+        assert piece >= 1
+        spans = [(i * piece, min(B, (i + 1) * piece)) for i in range(n)]
+        covered = [b for lo, hi in spans for b in range(lo, hi)] if B <= 10000 else None
+        if covered is not None:
+            assert covered == list(range(B))
+        assert all(hi > lo for lo, hi in spans)
+        assert piece * doc <= budget or piece == 1
+        assert n == (0 if B == 0 else -(-B // piece))
